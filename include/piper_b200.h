@@ -1,0 +1,129 @@
+/*
+ * piper_b200 -- C ABI of the B200 (sm_100a) backend of Piper Attention.
+ *
+ * This is the boundary the Python operator binds (through ctypes) and that
+ * any other host language can bind the same way.  Signatures use only plain
+ * pointers, integers and sizes: no torch, no C++ types.  No C++ exception
+ * crosses it; every entry point returns a piper_b200_status and, on failure,
+ * records a message readable with piper_b200_last_error().
+ *
+ * Reference interfaces replaced (Piper Kernels 0.2.1, paths inside the
+ * project):
+ *   piper_b200_attention_fwd       <- torch.ops.piper_kernels.piper_attention
+ *                                     src/piper_kernels/attention/piper_attention/triton.py:984-999
+ *                                     (== _run_piper_attention, triton.py:954-981)
+ *   piper_b200_prepass             <- _prepare_piper_attention, triton.py:772-890
+ *                                     (_compute_kv_means 638-699, prepare_query/prepare_key
+ *                                     qk_quantization/int8/sage/triton.py:238-356,
+ *                                     _quantize_value_per_key_kernel triton.py:176-246)
+ *   piper_b200_attention_prepared  <- _launch_piper_attention, triton.py:893-951
+ *   piper_b200_workspace_bytes /
+ *   piper_b200_workspace_layout    <- the per-call torch allocations of triton.py:814-838, 874
+ *                                     (the caller owns the memory here)
+ *   piper_b200_supports_device     <- AcceleratorTarget.supports_uint8_int8_mma,
+ *                                     src/piper_kernels/_triton/targets.py:100-104
+ *
+ * Conventions:
+ *   - q/k/v are [B, H, N, D] with the head dimension contiguous; strides[3]
+ *     are the B, H and N strides in ELEMENTS (arbitrary, like the reference's
+ *     strided-input contract, src/piper_kernels/attention/_validation.py:12-23).
+ *   - out is a contiguous [B, H, Nq, D] tensor of the input dtype.
+ *   - dtype: PIPER_B200_FLOAT16 or PIPER_B200_BFLOAT16; D in {64, 128};
+ *     causal requires Nq == Nk (the Python layer validates first, with the
+ *     reference's messages; these checks are the backstop).
+ *   - stream is a cudaStream_t (NULL = legacy default stream).  Nothing here
+ *     synchronises the host.
+ *   - workspace: caller-owned device memory of at least
+ *     piper_b200_workspace_bytes(...) bytes, 256-byte aligned.
+ */
+#ifndef PIPER_B200_H_
+#define PIPER_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum piper_b200_status {
+  PIPER_B200_OK = 0,
+  PIPER_B200_ERR_INVALID_ARGUMENT = 1,
+  PIPER_B200_ERR_UNSUPPORTED_DEVICE = 2,
+  PIPER_B200_ERR_CUDA = 3,
+  PIPER_B200_ERR_TIMEOUT = 4,
+  PIPER_B200_ERR_WORKSPACE_TOO_SMALL = 5
+} piper_b200_status;
+
+enum { PIPER_B200_FLOAT16 = 0, PIPER_B200_BFLOAT16 = 1 };
+
+/* Byte offsets of each intermediate inside the workspace (see layout.h in
+ * the sources for shapes).  Exposed so tests can read the INT8 codes and
+ * scales the prepass produced. */
+typedef struct piper_b200_workspace_layout_s {
+  uint64_t q8, k8, v8t, qscale, kscale, vscale, vlog2, vrcp, kmean, vmean, ksum, vsum, counter;
+  uint64_t total_bytes;
+  int64_t q_groups, k_groups, nk_pad, chunks;
+} piper_b200_workspace_layout_t;
+
+/* ABI version of this header (major*100 + minor). */
+int piper_b200_abi_version(void);
+
+/* Message of the most recent failure on the calling thread ("" if none). */
+const char* piper_b200_last_error(void);
+
+/* 1 when `device` is an sm_100 GPU this library was built for, else 0. */
+int piper_b200_supports_device(int device);
+
+int piper_b200_workspace_bytes(int64_t batch, int64_t heads, int64_t query_length,
+                               int64_t key_length, int64_t head_dim, size_t* bytes);
+
+int piper_b200_workspace_layout(int64_t batch, int64_t heads, int64_t query_length,
+                                int64_t key_length, int64_t head_dim,
+                                piper_b200_workspace_layout_t* layout);
+
+/* Quantization prepass: K/V sequence means, K smoothing, per-32-row Q and
+ * per-64-row K INT8 codes + scales, per-key-row V INT8 codes (centered by the
+ * V mean when non-causal) + scales, into the workspace. */
+int piper_b200_prepass(const void* query, const int64_t query_strides[3], const void* key,
+                       const int64_t key_strides[3], const void* value,
+                       const int64_t value_strides[3], int dtype, int64_t batch, int64_t heads,
+                       int64_t query_length, int64_t key_length, int64_t head_dim, int is_causal,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* The fused INT8-QK / UINT8xINT8-PV attention on a prepared workspace. */
+int piper_b200_attention_prepared(void* out, int dtype, int64_t batch, int64_t heads,
+                                  int64_t query_length, int64_t key_length, int64_t head_dim,
+                                  double scale, int is_causal, const void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* piper_b200_prepass followed by piper_b200_attention_prepared. */
+int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], const void* key,
+                             const int64_t key_strides[3], const void* value,
+                             const int64_t value_strides[3], void* out, int dtype, int64_t batch,
+                             int64_t heads, int64_t query_length, int64_t key_length,
+                             int64_t head_dim, double scale, int is_causal, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* Reads (and, if `clear`, resets) the device status word that kernels set when
+ * a bounded wait gave up.  Synchronises the device.  *status == 0 means no
+ * kernel of this library has timed out on `device`. */
+int piper_b200_device_status(int device, int clear, uint32_t* status);
+
+/* Self-test of the bounded-wait path: launches one CTA that waits on an
+ * mbarrier nothing ever arrives at, with a `budget_ns` limit, and reports
+ * whether it gave up cleanly (*timed_out = 1) while the context stays usable. */
+int piper_b200_selftest_wait_timeout(uint64_t budget_ns, int* timed_out, void* stream);
+
+/* Diagnostic GEMM on the tensor cores: C[M,N] (int32) = A[M,K] * B[N,K]^T with
+ * A u8 or s8 (a_signed), B s8, both K-major, through the same TMA + tcgen05
+ * kind::i8 path the attention kernel uses.  M % 128 == 0, N % 64 == 0,
+ * K % 128 == 0; all pointers are device memory. */
+int piper_b200_selftest_gemm_i8(const void* a, const void* b, int32_t* c, int64_t m, int64_t n,
+                                int64_t k, int a_signed, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PIPER_B200_H_ */

@@ -1,0 +1,63 @@
+// Workspace layout shared by the host launcher and the kernels.
+//
+// One contiguous caller-owned device buffer holds every intermediate of a
+// piper_attention call.  Region offsets are 256-byte aligned.  Sizes for a
+// problem (B,H,Nq,Nk,D) with BH = B*H:
+//   q8      int8  [BH, Nq, D]                 Q codes (row-major, per-32-row scale)
+//   k8      int8  [BH, Nk, D]                 centered-K codes (per-64-row scale)
+//   v8t     int8  [BH, D, Nk_pad]             V codes transposed: keys contiguous
+//   qscale  f32   [BH, ceil(Nq/32)]           Q group scales   (reference: query_scale)
+//   kscale  f32   [BH, ceil(Nk/64)]           K group scales   (reference: key_scale)
+//   vscale  f32   [BH, Nk_pad]                V row scales     (reference: value_scale)
+//   vlog2   f32   [BH, Nk_pad]                log2(vscale); -inf on padded keys
+//   vrcp    f32   [BH, Nk_pad]                1/vscale; 0 on padded keys
+//   kmean   f32   [BH, D]                     K sequence mean
+//   vmean   f32   [BH, D]                     V sequence mean (zeros when causal)
+//   ksum    f64   [BH, chunks, D]             per-chunk partial sums of K
+//   vsum    f64   [BH, chunks, D]             per-chunk partial sums of V
+//   counter u32   [BH]                        chunk-completion counters
+// with Nk_pad = roundup(Nk, 64) and chunks = ceil(Nk / kSumChunkRows).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "piper_b200.h"
+
+namespace piper {
+constexpr int kQueryGroup = 32;     // rows per Q scale (per_warp granularity)
+constexpr int kKeyGroup = 64;       // rows per K scale
+constexpr int kKeyBlock = 64;       // keys per online-softmax block (PV block)
+constexpr int kSumChunkRows = 512;  // rows per partial-sum chunk of the mean pass
+
+inline uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+inline piper_b200_workspace_layout_t make_layout(int64_t bh, int64_t nq, int64_t nk, int64_t d) {
+  piper_b200_workspace_layout_t L{};
+  L.q_groups = (nq + kQueryGroup - 1) / kQueryGroup;
+  L.k_groups = (nk + kKeyGroup - 1) / kKeyGroup;
+  L.nk_pad = (nk + kKeyBlock - 1) / kKeyBlock * kKeyBlock;
+  L.chunks = (nk + kSumChunkRows - 1) / kSumChunkRows;
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) {
+    uint64_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  L.q8 = take(static_cast<uint64_t>(bh * nq * d));
+  L.k8 = take(static_cast<uint64_t>(bh * nk * d));
+  L.v8t = take(static_cast<uint64_t>(bh * d * L.nk_pad));
+  L.qscale = take(static_cast<uint64_t>(bh * L.q_groups) * 4);
+  L.kscale = take(static_cast<uint64_t>(bh * L.k_groups) * 4);
+  L.vscale = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
+  L.vlog2 = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
+  L.vrcp = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
+  L.kmean = take(static_cast<uint64_t>(bh * d) * 4);
+  L.vmean = take(static_cast<uint64_t>(bh * d) * 4);
+  L.ksum = take(static_cast<uint64_t>(bh * L.chunks * d) * 8);
+  L.vsum = take(static_cast<uint64_t>(bh * L.chunks * d) * 8);
+  L.counter = take(static_cast<uint64_t>(bh) * 4);
+  L.total_bytes = off;
+  return L;
+}
+}  // namespace piper

@@ -1,0 +1,364 @@
+// C ABI of the B200 Piper Attention backend (declared in include/piper_b200.h).
+//
+// Host orchestration that replaces the reference's Triton launch sequence
+// (Piper Kernels 0.2.1, attention/piper_attention/triton.py:772-981):
+// argument checks, per-device one-time set-up, TMA tensor-map encoding and
+// the three kernel launches, all on the caller's stream with no host sync.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "attention.cuh"
+#include "layout.h"
+#include "piper_b200.h"
+#include "prepass.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(PIPER_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+#define PIPER_CUDA(call)                                   \
+  do {                                                     \
+    cudaError_t e_ = (call);                               \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);    \
+  } while (0)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kMaxDevices = 64;
+std::mutex g_init_mutex;
+bool g_device_ready[kMaxDevices] = {};
+EncodeTiledFn g_encode = nullptr;
+
+// One-time per-device set-up (thread safe): architecture check and the
+// dynamic shared-memory opt-in of the attention kernels.
+int ensure_device(int* device_out) {
+  int device = 0;
+  PIPER_CUDA(cudaGetDevice(&device));
+  if (device < 0 || device >= kMaxDevices) return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE, "device index out of range");
+  *device_out = device;
+  std::lock_guard<std::mutex> lock(g_init_mutex);
+  if (g_device_ready[device]) return PIPER_B200_OK;
+  cudaDeviceProp prop;
+  PIPER_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE,
+                "piper_b200 requires an sm_100 (B200-class) GPU, got sm_" + std::to_string(prop.major) +
+                    std::to_string(prop.minor));
+  if (g_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    PIPER_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return fail(PIPER_B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__half, 64>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<64>::kAlloc));
+  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__half, 128>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<128>::kAlloc));
+  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__nv_bfloat16, 64>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<64>::kAlloc));
+  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__nv_bfloat16, 128>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<128>::kAlloc));
+  g_device_ready[device] = true;
+  return PIPER_B200_OK;
+}
+
+// 3-D int8 tensor map: dims {inner, mid, outer} with byte strides
+// {mid_stride, outer_stride}, a box {box_inner, box_mid, 1} and the swizzle
+// matching box_inner (64 or 128 bytes).
+int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t mid, uint64_t outer,
+               uint64_t mid_stride, uint64_t outer_stride, uint32_t box_inner, uint32_t box_mid) {
+  const cuuint64_t dims[3] = {inner, mid, outer};
+  const cuuint64_t strides[2] = {mid_stride, outer_stride};
+  const cuuint32_t box[3] = {box_inner, box_mid, 1};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = box_inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PIPER_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return PIPER_B200_OK;
+}
+
+int check_shape(int dtype, int64_t b, int64_t h, int64_t nq, int64_t nk, int64_t d, int causal) {
+  if (dtype != PIPER_B200_FLOAT16 && dtype != PIPER_B200_BFLOAT16)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "dtype must be PIPER_B200_FLOAT16 or PIPER_B200_BFLOAT16");
+  if (d != 64 && d != 128)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "head_dim must be 64 or 128, got " + std::to_string(d));
+  if (b <= 0 || h <= 0) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "batch and heads must be positive");
+  if (nq <= 0 || nk <= 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "query and key lengths must be positive");
+  if (causal && nq != nk)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "causal attention requires equal query and key lengths");
+  if (b * h > 65535) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "batch*heads must be at most 65535");
+  if (nq > (int64_t(1) << 30) || nk > (int64_t(1) << 30))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "sequence lengths must be below 2^30");
+  return PIPER_B200_OK;
+}
+
+bool aligned16(const void* p, const int64_t s[3]) {
+  return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && s[0] % 8 == 0 && s[1] % 8 == 0 && s[2] % 8 == 0;
+}
+
+template <typename T, int D, bool V16>
+void launch_prepass_t(const piper::PrepassArgs& a, int64_t bh, cudaStream_t stream) {
+  const dim3 sum_grid(static_cast<unsigned>(a.L.chunks), static_cast<unsigned>(bh));
+  piper::kv_sum_kernel<T, D, V16><<<sum_grid, piper::kPrepassThreads, 0, stream>>>(a);
+  const int64_t tiles = (std::max(a.nq, a.nk) + piper::kKeyBlock - 1) / piper::kKeyBlock;
+  const dim3 q_grid(static_cast<unsigned>(tiles), static_cast<unsigned>(bh));
+  piper::quantize_kernel<T, D, V16><<<q_grid, piper::kPrepassThreads, 0, stream>>>(a);
+}
+
+template <typename T, int D>
+void launch_prepass_d(const piper::PrepassArgs& a, int64_t bh, bool v16, cudaStream_t stream) {
+  if (v16)
+    launch_prepass_t<T, D, true>(a, bh, stream);
+  else
+    launch_prepass_t<T, D, false>(a, bh, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int piper_b200_abi_version(void) { return 100; }
+
+const char* piper_b200_last_error(void) { return g_last_error.c_str(); }
+
+int piper_b200_supports_device(int device) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return (prop.major == 10 && prop.minor == 0) ? 1 : 0;
+}
+
+int piper_b200_workspace_layout(int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                                int64_t head_dim, piper_b200_workspace_layout_t* layout) {
+  if (layout == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "layout is NULL");
+  if (batch <= 0 || heads <= 0 || query_length <= 0 || key_length <= 0 || head_dim <= 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  *layout = piper::make_layout(batch * heads, query_length, key_length, head_dim);
+  return PIPER_B200_OK;
+}
+
+int piper_b200_workspace_bytes(int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                               int64_t head_dim, size_t* bytes) {
+  piper_b200_workspace_layout_t L;
+  const int rc = piper_b200_workspace_layout(batch, heads, query_length, key_length, head_dim, &L);
+  if (rc != PIPER_B200_OK) return rc;
+  if (bytes == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  *bytes = static_cast<size_t>(L.total_bytes);
+  return PIPER_B200_OK;
+}
+
+int piper_b200_prepass(const void* query, const int64_t query_strides[3], const void* key,
+                       const int64_t key_strides[3], const void* value, const int64_t value_strides[3], int dtype,
+                       int64_t batch, int64_t heads, int64_t query_length, int64_t key_length, int64_t head_dim,
+                       int is_causal, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!query || !key || !value || !workspace || !query_strides || !key_strides || !value_strides)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
+  if (workspace_bytes < L.total_bytes)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
+                "workspace needs " + std::to_string(L.total_bytes) + " bytes, got " + std::to_string(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  piper::PrepassArgs a{};
+  a.q = query;
+  a.k = key;
+  a.v = value;
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = query_strides[i];
+    a.ks[i] = key_strides[i];
+    a.vs[i] = value_strides[i];
+  }
+  a.heads = heads;
+  a.nq = query_length;
+  a.nk = key_length;
+  a.causal = is_causal ? 1 : 0;
+  a.ws = static_cast<uint8_t*>(workspace);
+  a.L = L;
+  const bool v16 = aligned16(query, query_strides) && aligned16(key, key_strides) && aligned16(value, value_strides);
+  PIPER_CUDA(cudaMemsetAsync(a.ws + L.counter, 0, static_cast<size_t>(bh) * 4, s));
+  if (dtype == PIPER_B200_FLOAT16) {
+    if (head_dim == 64)
+      launch_prepass_d<__half, 64>(a, bh, v16, s);
+    else
+      launch_prepass_d<__half, 128>(a, bh, v16, s);
+  } else {
+    if (head_dim == 64)
+      launch_prepass_d<__nv_bfloat16, 64>(a, bh, v16, s);
+    else
+      launch_prepass_d<__nv_bfloat16, 128>(a, bh, v16, s);
+  }
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
+}
+
+int piper_b200_attention_prepared(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                                  int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                                  const void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!out || !workspace) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  if (!(std::isfinite(scale) && scale > 0.0))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "scale must be finite and positive");
+  if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "output must be 16-byte aligned");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
+  if (workspace_bytes < L.total_bytes)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "workspace too small for this problem");
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  const uint64_t d = static_cast<uint64_t>(head_dim);
+  CUtensorMap tmQ, tmK, tmV;
+  if ((rc = encode_map(&tmQ, ws + L.q8, d, query_length, bh, d, query_length * d, static_cast<uint32_t>(d),
+                       piper::kTileM)) != PIPER_B200_OK)
+    return rc;
+  if ((rc = encode_map(&tmK, ws + L.k8, d, key_length, bh, d, key_length * d, static_cast<uint32_t>(d),
+                       piper::kKeyBlock)) != PIPER_B200_OK)
+    return rc;
+  if ((rc = encode_map(&tmV, ws + L.v8t, L.nk_pad, d, bh, L.nk_pad, L.nk_pad * d, piper::kKeyBlock,
+                       static_cast<uint32_t>(d))) != PIPER_B200_OK)
+    return rc;
+  piper::AttnParams p{};
+  p.qscale = reinterpret_cast<const float*>(ws + L.qscale);
+  p.kscale = reinterpret_cast<const float*>(ws + L.kscale);
+  p.vlog2 = reinterpret_cast<const float*>(ws + L.vlog2);
+  p.vrcp = reinterpret_cast<const float*>(ws + L.vrcp);
+  p.vmean = reinterpret_cast<const float*>(ws + L.vmean);
+  p.out = out;
+  p.heads = heads;
+  p.nq = query_length;
+  p.nk = key_length;
+  p.nk_pad = L.nk_pad;
+  p.q_groups = L.q_groups;
+  p.k_groups = L.k_groups;
+  p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
+  p.causal = is_causal ? 1 : 0;
+  p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
+  p.wait_budget_ns = piper::kWaitBudgetNs;
+  const dim3 grid(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PIPER_B200_FLOAT16) {
+    if (head_dim == 64)
+      piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+    else
+      piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+  } else {
+    if (head_dim == 64)
+      piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+    else
+      piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+  }
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
+}
+
+int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], const void* key,
+                             const int64_t key_strides[3], const void* value, const int64_t value_strides[3],
+                             void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                             int64_t key_length, int64_t head_dim, double scale, int is_causal, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  int rc = piper_b200_prepass(query, query_strides, key, key_strides, value, value_strides, dtype, batch, heads,
+                              query_length, key_length, head_dim, is_causal, workspace, workspace_bytes, stream);
+  if (rc != PIPER_B200_OK) return rc;
+  return piper_b200_attention_prepared(out, dtype, batch, heads, query_length, key_length, head_dim, scale,
+                                       is_causal, workspace, workspace_bytes, stream);
+}
+
+int piper_b200_device_status(int device, int clear, uint32_t* status) {
+  if (status == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "status is NULL");
+  int prev = 0;
+  PIPER_CUDA(cudaGetDevice(&prev));
+  PIPER_CUDA(cudaSetDevice(device));
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status, piper::g_piper_status, sizeof(uint32_t));
+  if (e == cudaSuccess && clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(piper::g_piper_status, &zero, sizeof(uint32_t));
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device status word");
+  return PIPER_B200_OK;
+}
+
+int piper_b200_selftest_wait_timeout(uint64_t budget_ns, int* timed_out, void* stream) {
+  if (timed_out == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "timed_out is NULL");
+  if (budget_ns > 10ull * 1000 * 1000 * 1000) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "budget above 10 s");
+  int device = 0;
+  int rc = ensure_device(&device);
+  if (rc != PIPER_B200_OK) return rc;
+  int* d_flag = nullptr;
+  uint32_t* d_status = nullptr;
+  PIPER_CUDA(cudaMalloc(&d_flag, sizeof(int)));
+  cudaError_t e = cudaMalloc(&d_status, sizeof(uint32_t));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(d_flag, 0xff, sizeof(int), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
+  if (e == cudaSuccess) {
+    piper::selftest_wait_kernel<<<1, 32, 0, s>>>(budget_ns, d_flag, d_status);
+    e = cudaGetLastError();
+  }
+  int host_flag = -1;
+  uint32_t host_status = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&host_flag, d_flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&host_status, d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(d_flag);
+  if (d_status) cudaFree(d_status);
+  if (e != cudaSuccess) return cuda_fail(e, "wait-timeout self-test");
+  *timed_out = (host_flag == 1 && (host_status & piper::kStatusTimeoutProbe)) ? 1 : 0;
+  return PIPER_B200_OK;
+}
+
+int piper_b200_selftest_gemm_i8(const void* a, const void* b, int32_t* c, int64_t m, int64_t n, int64_t k,
+                                int a_signed, void* stream) {
+  if (!a || !b || !c) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  if (m <= 0 || n <= 0 || k <= 0 || m % 128 || n % 64 || k % 128)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "need M%128 == 0, N%64 == 0, K%128 == 0");
+  int device = 0;
+  int rc = ensure_device(&device);
+  if (rc != PIPER_B200_OK) return rc;
+  CUtensorMap tmA, tmB;
+  if ((rc = encode_map(&tmA, a, k, m, 1, k, m * k, 128, 128)) != PIPER_B200_OK) return rc;
+  if ((rc = encode_map(&tmB, b, k, n, 1, k, n * k, 128, 64)) != PIPER_B200_OK) return rc;
+  const dim3 grid(static_cast<unsigned>(m / 128), static_cast<unsigned>(n / 64));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a_signed)
+    piper::selftest_gemm_kernel<true><<<grid, 128, 0, s>>>(tmA, tmB, c, n, k, piper::kWaitBudgetNs);
+  else
+    piper::selftest_gemm_kernel<false><<<grid, 128, 0, s>>>(tmA, tmB, c, n, k, piper::kWaitBudgetNs);
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
+}
+
+}  // extern "C"

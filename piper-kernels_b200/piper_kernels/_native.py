@@ -1,0 +1,144 @@
+"""ctypes binding of the C ABI in ``include/piper_b200.h`` (``libpiper_b200.so``).
+
+The library is built in-tree by ``piper-kernels_b200/build.py`` (or
+``__graft_entry__.build()``) into ``piper_kernels/_lib/``.  There is no
+fallback: if the shared library is missing, every entry point raises
+:class:`NativeLibraryMissing` with the build instructions.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_DIR = Path(__file__).resolve().parent / "_lib"
+LIB_PATH = LIB_DIR / "libpiper_b200.so"
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED_DEVICE = 2
+ERR_CUDA = 3
+ERR_TIMEOUT = 4
+ERR_WORKSPACE_TOO_SMALL = 5
+FLOAT16 = 0
+BFLOAT16 = 1
+
+# Every symbol include/piper_b200.h declares (tests check the library exports them).
+EXPORTED_SYMBOLS = (
+    "piper_b200_abi_version",
+    "piper_b200_last_error",
+    "piper_b200_supports_device",
+    "piper_b200_workspace_bytes",
+    "piper_b200_workspace_layout",
+    "piper_b200_prepass",
+    "piper_b200_attention_prepared",
+    "piper_b200_attention_fwd",
+    "piper_b200_device_status",
+    "piper_b200_selftest_wait_timeout",
+    "piper_b200_selftest_gemm_i8",
+)
+
+
+class NativeLibraryMissing(RuntimeError):
+    """The compiled sm_100a library is not present next to the package."""
+
+
+class WorkspaceLayout(ctypes.Structure):
+    """Mirror of ``piper_b200_workspace_layout_t``."""
+
+    _fields_ = [
+        (name, ctypes.c_uint64)
+        for name in (
+            "q8", "k8", "v8t", "qscale", "kscale", "vscale", "vlog2", "vrcp",
+            "kmean", "vmean", "ksum", "vsum", "counter", "total_bytes",
+        )
+    ] + [(name, ctypes.c_int64) for name in ("q_groups", "k_groups", "nk_pad", "chunks")]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+_I64 = ctypes.c_int64
+_STRIDES = ctypes.c_int64 * 3
+_VP = ctypes.c_void_p
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    lib.piper_b200_abi_version.restype = ctypes.c_int
+    lib.piper_b200_last_error.restype = ctypes.c_char_p
+    lib.piper_b200_supports_device.argtypes = [ctypes.c_int]
+    lib.piper_b200_supports_device.restype = ctypes.c_int
+    lib.piper_b200_workspace_bytes.argtypes = [_I64] * 5 + [ctypes.POINTER(ctypes.c_size_t)]
+    lib.piper_b200_workspace_bytes.restype = ctypes.c_int
+    lib.piper_b200_workspace_layout.argtypes = [_I64] * 5 + [ctypes.POINTER(WorkspaceLayout)]
+    lib.piper_b200_workspace_layout.restype = ctypes.c_int
+    tensor3 = [_VP, _STRIDES] * 3
+    lib.piper_b200_prepass.argtypes = tensor3 + [ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_prepass.restype = ctypes.c_int
+    lib.piper_b200_attention_prepared.argtypes = [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_attention_prepared.restype = ctypes.c_int
+    lib.piper_b200_attention_fwd.argtypes = tensor3 + [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_attention_fwd.restype = ctypes.c_int
+    lib.piper_b200_device_status.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
+    lib.piper_b200_device_status.restype = ctypes.c_int
+    lib.piper_b200_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int), _VP]
+    lib.piper_b200_selftest_wait_timeout.restype = ctypes.c_int
+    lib.piper_b200_selftest_gemm_i8.argtypes = [_VP, _VP, _VP] + [_I64] * 3 + [ctypes.c_int, _VP]
+    lib.piper_b200_selftest_gemm_i8.restype = ctypes.c_int
+
+
+def library() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it was never built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise NativeLibraryMissing(
+                    f"{LIB_PATH} is missing: build the sm_100a extension with "
+                    "`python piper-kernels_b200/build.py` (or __graft_entry__.build())"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            _declare(lib)
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    return library().piper_b200_last_error().decode("utf-8", "replace")
+
+
+def check(status: int, what: str) -> None:
+    """Raise the Python exception matching a piper_b200_status."""
+    if status == OK:
+        return
+    message = f"{what}: {last_error()}"
+    if status in (ERR_INVALID_ARGUMENT, ERR_WORKSPACE_TOO_SMALL):
+        raise ValueError(message)
+    if status == ERR_TIMEOUT:
+        raise TimeoutError(message)
+    raise RuntimeError(message)
+
+
+def strides3(tensor) -> _STRIDES:
+    s = tensor.stride()
+    return _STRIDES(s[0], s[1], s[2])
+
+
+def workspace_layout(batch: int, heads: int, nq: int, nk: int, d: int) -> WorkspaceLayout:
+    layout = WorkspaceLayout()
+    check(library().piper_b200_workspace_layout(batch, heads, nq, nk, d, ctypes.byref(layout)), "workspace layout")
+    return layout
+
+
+def device_status(device: int, clear: bool = True) -> int:
+    value = ctypes.c_uint32(0)
+    check(library().piper_b200_device_status(device, 1 if clear else 0, ctypes.byref(value)), "device status")
+    return int(value.value)

@@ -1,0 +1,5 @@
+"""Piper Attention: public operator and its B200 backend."""
+
+from .dispatch import piper_attention
+
+__all__ = ["piper_attention"]

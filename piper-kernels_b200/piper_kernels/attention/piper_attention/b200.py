@@ -1,0 +1,209 @@
+"""B200 backend of Piper Attention: custom op over the sm_100a C ABI.
+
+Replaces the reference's Triton backend
+(Piper Kernels 0.2.1, ``src/piper_kernels/attention/piper_attention/triton.py``):
+
+* ``torch.ops.piper_kernels.piper_attention(query, key, value, scale, is_causal)``
+  is registered with the same name, schema and fake implementation
+  (triton.py:984-1010), so ``torch.compile(fullgraph=True)`` traces it as one
+  opaque op;
+* ``prepare_piper_attention`` / ``launch_piper_attention`` reproduce the
+  reference's prepare/launch split (triton.py:772-951) used by benchmarks;
+* all device memory (output and one workspace holding every intermediate)
+  is allocated here through torch's caching allocator on the query's device,
+  and the kernels run on the current torch stream of that device.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ... import _native
+
+_DTYPE_CODES = {torch.float16: _native.FLOAT16, torch.bfloat16: _native.BFLOAT16}
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@dataclass(frozen=True)
+class PreparedPiperAttention:
+    """Workspace of one call plus typed views of its intermediates.
+
+    The views alias ``workspace``; they match the reference's prepared tensors
+    (triton.py:754-769) except that V codes are stored transposed
+    ``[B,H,D,Nk_pad]`` and scales are per group (``[B,H,ceil(N/32|64)]``).
+    """
+
+    workspace: torch.Tensor
+    layout: _native.WorkspaceLayout
+    shape: tuple[int, int, int, int, int]  # B, H, Nq, Nk, D
+    dtype: torch.dtype
+    is_causal: bool
+
+    def _view(self, offset: int, count: int, dtype: torch.dtype, shape: tuple[int, ...]) -> torch.Tensor:
+        nbytes = count * torch.empty((), dtype=dtype).element_size()
+        return self.workspace[offset : offset + nbytes].view(dtype).view(shape)
+
+    @property
+    def query_int8(self) -> torch.Tensor:
+        b, h, nq, _nk, d = self.shape
+        return self._view(self.layout.q8, b * h * nq * d, torch.int8, (b, h, nq, d))
+
+    @property
+    def key_int8(self) -> torch.Tensor:
+        b, h, _nq, nk, d = self.shape
+        return self._view(self.layout.k8, b * h * nk * d, torch.int8, (b, h, nk, d))
+
+    @property
+    def value_int8_transposed(self) -> torch.Tensor:
+        b, h, _nq, _nk, d = self.shape
+        pad = self.layout.nk_pad
+        return self._view(self.layout.v8t, b * h * d * pad, torch.int8, (b, h, d, pad))
+
+    @property
+    def value_int8(self) -> torch.Tensor:
+        """V codes in the reference's ``[B,H,Nk,D]`` orientation (a copy)."""
+        nk = self.shape[3]
+        return self.value_int8_transposed[..., :nk].transpose(-1, -2).contiguous()
+
+    @property
+    def query_scale(self) -> torch.Tensor:
+        b, h = self.shape[:2]
+        g = self.layout.q_groups
+        return self._view(self.layout.qscale, b * h * g, torch.float32, (b, h, g))
+
+    @property
+    def key_scale(self) -> torch.Tensor:
+        b, h = self.shape[:2]
+        g = self.layout.k_groups
+        return self._view(self.layout.kscale, b * h * g, torch.float32, (b, h, g))
+
+    @property
+    def value_scale(self) -> torch.Tensor:
+        b, h, _nq, nk, _d = self.shape
+        pad = self.layout.nk_pad
+        return self._view(self.layout.vscale, b * h * pad, torch.float32, (b, h, pad))[..., :nk]
+
+    @property
+    def key_mean(self) -> torch.Tensor:
+        b, h, _nq, _nk, d = self.shape
+        return self._view(self.layout.kmean, b * h * d, torch.float32, (b, h, d))
+
+    @property
+    def value_mean(self) -> torch.Tensor:
+        b, h, _nq, _nk, d = self.shape
+        return self._view(self.layout.vmean, b * h * d, torch.float32, (b, h, d))
+
+
+def workspace_bytes(batch: int, heads: int, nq: int, nk: int, d: int) -> int:
+    return int(_native.workspace_layout(batch, heads, nq, nk, d).total_bytes)
+
+
+def prepare_piper_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    is_causal: bool,
+    *,
+    workspace: torch.Tensor | None = None,
+) -> PreparedPiperAttention:
+    """Run the quantization prepass into a (new or given) workspace."""
+    lib = _native.library()
+    b, h, nq, d = query.shape
+    nk = key.shape[2]
+    layout = _native.workspace_layout(b, h, nq, nk, d)
+    if workspace is None:
+        workspace = torch.empty(int(layout.total_bytes), dtype=torch.uint8, device=query.device)
+    with torch.cuda.device(query.device):
+        _native.check(
+            lib.piper_b200_prepass(
+                _ptr(query), _native.strides3(query), _ptr(key), _native.strides3(key),
+                _ptr(value), _native.strides3(value), _DTYPE_CODES[query.dtype],
+                b, h, nq, nk, d, 1 if is_causal else 0,
+                _ptr(workspace), workspace.numel(), _stream(query.device),
+            ),
+            "piper_b200_prepass",
+        )
+    return PreparedPiperAttention(workspace, layout, (b, h, nq, nk, d), query.dtype, is_causal)
+
+
+def launch_piper_attention(
+    prepared: PreparedPiperAttention,
+    scale: float,
+    *,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Run only the fused attention kernel on a prepared workspace."""
+    lib = _native.library()
+    b, h, nq, nk, d = prepared.shape
+    device = prepared.workspace.device
+    if out is None:
+        out = torch.empty((b, h, nq, d), dtype=prepared.dtype, device=device)
+    with torch.cuda.device(device):
+        _native.check(
+            lib.piper_b200_attention_prepared(
+                _ptr(out), _DTYPE_CODES[prepared.dtype], b, h, nq, nk, d, float(scale),
+                1 if prepared.is_causal else 0, _ptr(prepared.workspace), prepared.workspace.numel(),
+                _stream(device),
+            ),
+            "piper_b200_attention_prepared",
+        )
+    return out
+
+
+def run_piper_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    scale: float,
+    is_causal: bool,
+) -> torch.Tensor:
+    """Prepass + fused kernel in one C-ABI call (reference: _run_piper_attention)."""
+    lib = _native.library()
+    b, h, nq, d = query.shape
+    nk = key.shape[2]
+    layout = _native.workspace_layout(b, h, nq, nk, d)
+    workspace = torch.empty(int(layout.total_bytes), dtype=torch.uint8, device=query.device)
+    out = torch.empty((b, h, nq, d), dtype=query.dtype, device=query.device)
+    with torch.cuda.device(query.device):
+        _native.check(
+            lib.piper_b200_attention_fwd(
+                _ptr(query), _native.strides3(query), _ptr(key), _native.strides3(key),
+                _ptr(value), _native.strides3(value), _ptr(out), _DTYPE_CODES[query.dtype],
+                b, h, nq, nk, d, float(scale), 1 if is_causal else 0,
+                _ptr(workspace), workspace.numel(), _stream(query.device),
+            ),
+            "piper_b200_attention_fwd",
+        )
+    return out
+
+
+@torch.library.custom_op("piper_kernels::piper_attention", mutates_args=())
+def b200_piper_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    scale: float,
+    is_causal: bool,
+) -> torch.Tensor:
+    """Quantization prepass and fused INT8-QK / UINT8xINT8-PV attention on sm_100a."""
+    return run_piper_attention(query, key, value, scale, is_causal)
+
+
+@b200_piper_attention.register_fake
+def _b200_piper_attention_fake(
+    query: torch.Tensor,
+    _key: torch.Tensor,
+    _value: torch.Tensor,
+    _scale: float,
+    _is_causal: bool,
+) -> torch.Tensor:
+    return torch.empty_like(query, memory_format=torch.contiguous_format)
