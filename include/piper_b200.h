@@ -105,6 +105,34 @@ int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], 
                              int64_t head_dim, double scale, int is_causal, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Scratch capacity of piper_b200_attention_fwd_no_alloc: 16 MiB per GPU. */
+#define PIPER_B200_NO_ALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)
+
+/* The same forward pass as piper_b200_attention_fwd, for callers that cannot
+ * allocate device memory.  Examples: a plugin inside a host process that owns
+ * the whole GPU memory budget and refuses outside allocations; a binding from
+ * a language runtime that can hand over input and output pointers but has no
+ * device allocator; a steady-state loop where a cudaMalloc, which may
+ * synchronise the device, is not allowed.  It has no counterpart in the
+ * reference, which always allocates through torch.
+ *
+ * The caller still passes inputs and output.  The scratch comes from a
+ * fixed 16 MiB array (PIPER_B200_NO_ALLOC_WORKSPACE_BYTES) compiled into this
+ * library: every GPU that loads the library holds that array until the
+ * process exits.  A problem whose workspace (piper_b200_workspace_bytes)
+ * exceeds it is rejected with PIPER_B200_ERR_WORKSPACE_TOO_SMALL; no cudaMalloc,
+ * cudaFree or other allocating call is made.  The first call on a device looks
+ * up the array's device address for that device (make that first call before
+ * any stream capture).  All calls on a device share the one array, so two
+ * calls whose work overlaps on the GPU (different streams, no ordering
+ * between them) race and corrupt each other; order such calls on one stream. */
+int piper_b200_attention_fwd_no_alloc(const void* query, const int64_t query_strides[3],
+                                      const void* key, const int64_t key_strides[3],
+                                      const void* value, const int64_t value_strides[3], void* out,
+                                      int dtype, int64_t batch, int64_t heads,
+                                      int64_t query_length, int64_t key_length, int64_t head_dim,
+                                      double scale, int is_causal, void* stream);
+
 /* Reads (and, if `clear`, resets) the device status word that kernels set when
  * a bounded wait gave up.  Synchronises the device.  *status == 0 means no
  * kernel of this library has timed out on `device`. */

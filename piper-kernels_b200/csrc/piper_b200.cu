@@ -362,3 +362,61 @@ int piper_b200_selftest_gemm_i8(const void* a, const void* b, int32_t* c, int64_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward pass without any device allocation (piper_b200_attention_fwd_no_alloc).
+//
+// For callers that cannot allocate device memory: the scratch lives in this
+// fixed file-scope array instead of a caller-provided workspace.  Host code
+// must not hand the array's name to a kernel (on the host it is only a
+// stand-in symbol); the device address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, and passed down as an
+// ordinary pointer.  The existing forward path then runs unchanged on it;
+// that path already clears the only region that must start at zero (the
+// mean-pass counters) on every call, so leftovers of an earlier call on the
+// shared array do no harm.  Calls that overlap on the GPU share the array and
+// race.
+namespace {
+
+static __device__ __align__(256) uint8_t g_no_alloc_workspace[PIPER_B200_NO_ALLOC_WORKSPACE_BYTES];
+
+void* g_no_alloc_address[kMaxDevices] = {};
+
+int no_alloc_workspace(int device, void** ptr) {
+  std::lock_guard<std::mutex> lock(g_init_mutex);
+  if (g_no_alloc_address[device] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&address, g_no_alloc_workspace);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc workspace)");
+    if (address == nullptr || reinterpret_cast<uintptr_t>(address) % 256 != 0)
+      return fail(PIPER_B200_ERR_CUDA, "no-alloc workspace has no usable device address");
+    g_no_alloc_address[device] = address;
+  }
+  *ptr = g_no_alloc_address[device];
+  return PIPER_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int piper_b200_attention_fwd_no_alloc(const void* query, const int64_t query_strides[3], const void* key,
+                                                 const int64_t key_strides[3], const void* value,
+                                                 const int64_t value_strides[3], void* out, int dtype, int64_t batch,
+                                                 int64_t heads, int64_t query_length, int64_t key_length,
+                                                 int64_t head_dim, double scale, int is_causal, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  const piper_b200_workspace_layout_t L = piper::make_layout(batch * heads, query_length, key_length, head_dim);
+  if (L.total_bytes > PIPER_B200_NO_ALLOC_WORKSPACE_BYTES)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
+                "this problem needs " + std::to_string(L.total_bytes) +
+                    " bytes of scratch; piper_b200_attention_fwd_no_alloc holds at most " +
+                    std::to_string(PIPER_B200_NO_ALLOC_WORKSPACE_BYTES) +
+                    " bytes (use piper_b200_attention_fwd with a caller-provided workspace)");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  void* workspace = nullptr;
+  if ((rc = no_alloc_workspace(device, &workspace)) != PIPER_B200_OK) return rc;
+  return piper_b200_attention_fwd(query, query_strides, key, key_strides, value, value_strides, out, dtype, batch,
+                                  heads, query_length, key_length, head_dim, scale, is_causal, workspace,
+                                  PIPER_B200_NO_ALLOC_WORKSPACE_BYTES, stream);
+}

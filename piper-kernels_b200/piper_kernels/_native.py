@@ -23,6 +23,7 @@ ERR_TIMEOUT = 4
 ERR_WORKSPACE_TOO_SMALL = 5
 FLOAT16 = 0
 BFLOAT16 = 1
+NO_ALLOC_WORKSPACE_BYTES = 16 * 1024 * 1024  # PIPER_B200_NO_ALLOC_WORKSPACE_BYTES
 
 # Every symbol include/piper_b200.h declares (tests check the library exports them).
 EXPORTED_SYMBOLS = (
@@ -34,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "piper_b200_prepass",
     "piper_b200_attention_prepared",
     "piper_b200_attention_fwd",
+    "piper_b200_attention_fwd_no_alloc",
     "piper_b200_device_status",
     "piper_b200_selftest_wait_timeout",
     "piper_b200_selftest_gemm_i8",
@@ -85,6 +87,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
     ]
     lib.piper_b200_attention_fwd.restype = ctypes.c_int
+    lib.piper_b200_attention_fwd_no_alloc.argtypes = tensor3 + [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP,
+    ]
+    lib.piper_b200_attention_fwd_no_alloc.restype = ctypes.c_int
     lib.piper_b200_device_status.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
     lib.piper_b200_device_status.restype = ctypes.c_int
     lib.piper_b200_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int), _VP]
