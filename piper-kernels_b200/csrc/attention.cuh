@@ -93,22 +93,62 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// TMEM accumulators are pre-loaded with the bit pattern of 1.5*2^23 before
+// every MMA chain (which accumulates onto it), so an INT32 result v with
+// |v| < 2^22 reads back as the float 1.5*2^23 + v exactly: one packed
+// subtraction converts two values.
+constexpr uint32_t kBiasBits = 0x4B400000u;
+constexpr float kBias = 12582912.0f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: numerator rescaled only past 2^8 growth
+
+__device__ __forceinline__ float2 f2(uint32_t a, uint32_t b) {
+  return make_float2(__uint_as_float(a), __uint_as_float(b));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Writes the bias pattern into `cols` consecutive TMEM columns of this lane.
+template <int kCols>
+__device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
+#pragma unroll
+  for (int c = 0; c < kCols; c += 4) tmem_st4_same(taddr + c, kBiasBits);
+}
+
 // Folds the INT32 PV partial of block jj (in TMEM) into the fp32 numerator
-// held in registers: o = o * w_old + PV * w_cur/255 (reference.py:102, 113).
+// held in registers (reference.py:113; the reference's numerator *= old_weight
+// of reference.py:102 is applied lazily by the caller).  The accumulator is
+// read as the float bias + PV, and folded as is, o += (bias + PV) * w: one
+// packed FMA per two columns.  The caller repeats the same FMA on the bias
+// alone (bias_acc = fma(bias, w, bias_acc)) and subtracts bias_acc once in the
+// epilogue, so a zero PV cancels exactly (constant V is restored bit for bit);
+// otherwise the cost is fp32 rounding at the magnitude of bias * sum(w),
+// about 1e-4 of the output scale.
 template <int D>
-__device__ __forceinline__ bool fold_pv(float (&o)[D], uint64_t* full, uint64_t* free_bar, int jj,
-                                        uint32_t tm_pv, float w_old, float w_pv, int lane,
-                                        uint64_t budget, uint32_t* status, volatile int* abort_flag) {
+__device__ __forceinline__ bool fold_pv(float2 (&o)[D / 2], uint32_t full, uint32_t free_bar, int jj,
+                                        uint32_t tm_pv, float w, int lane, uint64_t budget, uint32_t* status,
+                                        uint32_t abort_flag) {
   if (!mbar_wait_warp(full, jj & 1, budget, status, kStatusTimeoutMma, abort_flag)) return false;
   tc_fence_after();
+  const float2 w2 = make_float2(w, w);
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    uint32_t v[32];
-    tmem_ld32(tm_pv + c * 32, v);
+  for (int c = 0; c < D / 64; ++c) {
+    uint32_t v0[32], v1[32];
+    tmem_ld32_split(tm_pv + c * 64, v0);
+    tmem_ld32_split(tm_pv + c * 64 + 32, v1);
     tmem_ld_wait();
+    // Re-arm these columns now; the store completes while the math runs.
+    tmem_fill_bias<64>(tm_pv + c * 64);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * w_old + exact_i2f(v[i]) * w_pv;
+    for (int i = 0; i < 16; ++i) {
+      o[c * 32 + i] = __ffma2_rn(f2(v0[2 * i], v0[2 * i + 1]), w2, o[c * 32 + i]);
+      o[c * 32 + 16 + i] = __ffma2_rn(f2(v1[2 * i], v1[2 * i + 1]), w2, o[c * 32 + 16 + i]);
+    }
   }
+  tmem_st_wait();
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(free_bar);
@@ -121,20 +161,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                            const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using S = AttnSmem<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;     // [tile][buf]
-  uint64_t* s_free = s_full + kTiles * 2;    // [tile][buf]
-  uint64_t* p_full = s_free + kTiles * 2;    // [tile][buf]
-  uint64_t* pv_full = p_full + kTiles * 2;   // [tile]
-  uint64_t* pv_free = pv_full + kTiles;      // [tile]
-  uint64_t* mma_done = pv_free + kTiles;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Align to 1024 B (the 128B-swizzle atom) while keeping the pointer derived
+  // from the shared array, so every access stays a 32-bit shared access.
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+  // Shared-window addresses of the barriers (8 bytes each) and flags.
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t q_full = sbase + S::kOffBar;
+  const uint32_t kv_full = q_full + 8;                    // [stage]
+  const uint32_t kv_empty = kv_full + 8 * kStages;        // [stage]
+  const uint32_t s_full = kv_empty + 8 * kStages;         // [tile][buf]
+  const uint32_t s_free = s_full + 8 * kTiles * 2;        // [tile][buf]
+  const uint32_t p_full = s_free + 8 * kTiles * 2;        // [tile][buf]
+  const uint32_t pv_full = p_full + 8 * kTiles * 2;       // [tile]
+  const uint32_t pv_free = pv_full + 8 * kTiles;          // [tile]
+  const uint32_t mma_done = pv_free + 8 * kTiles;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kOffMisc + 4);
+  const uint32_t abort_flag = sbase + S::kOffMisc + 4;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -161,20 +205,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(kv_full + 8 * s, 1);
+      mbar_init(kv_empty + 8 * s, 1);
     }
     for (int i = 0; i < kTiles * 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(s_full + 8 * i, 1);
+      mbar_init(s_free + 8 * i, 4);
+      mbar_init(p_full + 8 * i, 4);
     }
     for (int t = 0; t < kTiles; ++t) {
-      mbar_init(&pv_full[t], 1);
-      mbar_init(&pv_free[t], 4);
+      mbar_init(pv_full + 8 * t, 1);
+      mbar_init(pv_free + 8 * t, 4);
     }
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
+    flag_set(abort_flag, 0u);
     fence_mbarrier_init();
   }
   if (warp == 9) {
@@ -192,6 +236,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t budget = p.wait_budget_ns;
   uint32_t* status = &g_piper_status;
+  if (warp < 8) {
+    // Every MMA accumulates onto the bias pattern: arm both S buffers and the
+    // PV accumulator of this thread's lane before the first MMA.
+    const uint32_t lane_tm = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16) + (warp / 4) * 256;
+    tmem_fill_bias<2 * kKeyBlock>(lane_tm);
+    tmem_fill_bias<D>(lane_tm + 128);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
@@ -203,29 +258,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_arrive_expect_tx(q_full, q_bytes);
       for (int t = 0; t < kTiles; ++t)
         if (nb[t] > 0)
-          tma_load_3d(smem + S::kOffQ + t * S::kQBytes, &tmQ, q_full, 0,
+          tma_load_3d(sbase + S::kOffQ + t * S::kQBytes, &tmQ, q_full, 0,
                       static_cast<int>(q0 + t * kTileM), static_cast<int>(bh));
       const float* vlog2 = p.vlog2 + bh * p.nk_pad;
       const float* vrcp = p.vrcp + bh * p.nk_pad;
       int issued = 0;
       for (int j = 0; j < nb_max; ++j) {
         const int s = j % kStages;
-        if (!mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, budget, status, kStatusTimeoutEmpty,
+        if (!mbar_wait(kv_empty + 8 * (s), ((j / kStages) & 1) ^ 1, budget, status, kStatusTimeoutEmpty,
                        abort_flag))
           break;
-        uint64_t* fb = &kv_full[s];
+        const uint32_t fb = kv_full + 8 * (s);
         mbar_arrive_expect_tx(fb, S::kKBytes + S::kVBytes + S::kVecBytes);
-        tma_load_3d(smem + S::kOffK + s * S::kKBytes, &tmK, fb, 0, j * kKeyBlock, static_cast<int>(bh));
-        tma_load_3d(smem + S::kOffV + s * S::kVBytes, &tmV, fb, j * kKeyBlock, 0, static_cast<int>(bh));
-        uint8_t* vec = smem + S::kOffVec + s * S::kVecBytes;
+        tma_load_3d(sbase + S::kOffK + s * S::kKBytes, &tmK, fb, 0, j * kKeyBlock, static_cast<int>(bh));
+        tma_load_3d(sbase + S::kOffV + s * S::kVBytes, &tmV, fb, j * kKeyBlock, 0, static_cast<int>(bh));
+        const uint32_t vec = sbase + S::kOffVec + s * S::kVecBytes;
         bulk_load(vec, vlog2 + j * kKeyBlock, kKeyBlock * 4, fb);
         bulk_load(vec + kKeyBlock * 4, vrcp + j * kKeyBlock, kKeyBlock * 4, fb);
         ++issued;
       }
       // Drain: every copy this thread issued must land before the CTA exits.
       for (int j = max(0, issued - kStages); j < issued; ++j)
-        mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, budget, status, kStatusTimeoutDrain, nullptr);
-      mbar_wait(q_full, 0, budget, status, kStatusTimeoutDrain, nullptr);
+        mbar_wait(kv_full + 8 * (j % kStages), (j / kStages) & 1, budget, status, kStatusTimeoutDrain, 0u);
+      mbar_wait(q_full, 0, budget, status, kStatusTimeoutDrain, 0u);
     } else if (warp == 9 && lane == 0) {
       // ------------------------------------------------ MMA issuer
       constexpr uint32_t kIdescQK = umma_idesc_i8(true, true, kTileM, kKeyBlock);
@@ -234,26 +289,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       uint64_t descQ[kTiles];
       for (int t = 0; t < kTiles; ++t)
-        descQ[t] = umma_desc_kmajor(smem_u32(smem + S::kOffQ + t * S::kQBytes), D);
+        descQ[t] = umma_desc_kmajor(sbase + S::kOffQ + t * S::kQBytes, D);
       for (int j = 0; ok && j <= nb_max; ++j) {
         if (j < nb_max) {
           const int s = j % kStages;
-          if (!(ok = mbar_wait(&kv_full[s], (j / kStages) & 1, budget, status, kStatusTimeoutFull, abort_flag)))
+          if (!(ok = mbar_wait(kv_full + 8 * (s), (j / kStages) & 1, budget, status, kStatusTimeoutFull, abort_flag)))
             break;
           tc_fence_after();
-          const uint64_t descK = umma_desc_kmajor(smem_u32(smem + S::kOffK + s * S::kKBytes), D);
+          const uint64_t descK = umma_desc_kmajor(sbase + S::kOffK + s * S::kKBytes, D);
           for (int t = 0; t < kTiles; ++t) {
             if (j >= nb[t]) continue;
             const int buf = j & 1;
-            if (!(ok = mbar_wait(&s_free[t * 2 + buf], ((j >> 1) & 1) ^ 1, budget, status,
+            if (!(ok = mbar_wait(s_free + 8 * (t * 2 + buf), ((j >> 1) & 1) ^ 1, budget, status,
                                  kStatusTimeoutEmpty, abort_flag)))
               break;
             tc_fence_after();
             const uint32_t dcol = tmem_base + t * 256 + buf * kKeyBlock;
 #pragma unroll
             for (int kk = 0; kk < D / 32; ++kk)
-              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[t * 2 + buf]);
+              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, 1u);
+            umma_commit(s_full + 8 * (t * 2 + buf));
           }
           if (!ok) break;
         }
@@ -261,37 +316,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int jp = j - 1;
           const int sp = jp % kStages;
           const int bufp = jp & 1;
-          const uint64_t descV = umma_desc_kmajor(smem_u32(smem + S::kOffV + sp * S::kVBytes), kKeyBlock);
+          const uint64_t descV = umma_desc_kmajor(sbase + S::kOffV + sp * S::kVBytes, kKeyBlock);
           for (int t = 0; t < kTiles; ++t) {
             if (jp >= nb[t]) continue;
-            if (!(ok = mbar_wait(&p_full[t * 2 + bufp], (jp >> 1) & 1, budget, status, kStatusTimeoutFull,
+            if (!(ok = mbar_wait(p_full + 8 * (t * 2 + bufp), (jp >> 1) & 1, budget, status, kStatusTimeoutFull,
                                  abort_flag)))
               break;
-            if (!(ok = mbar_wait(&pv_free[t], (jp & 1) ^ 1, budget, status, kStatusTimeoutEmpty, abort_flag)))
+            if (!(ok = mbar_wait(pv_free + 8 * (t), (jp & 1) ^ 1, budget, status, kStatusTimeoutEmpty, abort_flag)))
               break;
             tc_fence_after();
             const uint64_t descP =
-                umma_desc_kmajor(smem_u32(smem + S::kOffP + (t * 2 + bufp) * S::kPBytes), kKeyBlock);
+                umma_desc_kmajor(sbase + S::kOffP + (t * 2 + bufp) * S::kPBytes, kKeyBlock);
             const uint32_t dcol = tmem_base + t * 256 + 128;
 #pragma unroll
             for (int kk = 0; kk < kKeyBlock / 32; ++kk)
-              umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, kk > 0 ? 1u : 0u);
-            umma_commit(&pv_full[t]);
+              umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, 1u);
+            umma_commit(pv_full + 8 * (t));
           }
           if (!ok) break;
-          umma_commit(&kv_empty[sp]);
+          umma_commit(kv_empty + 8 * (sp));
         }
       }
       // Everything issued must complete before TMEM is freed.
       umma_commit(mma_done);
-      mbar_wait(mma_done, 0, budget, status, kStatusTimeoutMma, nullptr);
+      mbar_wait(mma_done, 0, budget, status, kStatusTimeoutMma, 0u);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
     // -------------------------------------------------- softmax warpgroups
     const int t = warp / 4;
     const int r = threadIdx.x % kTileM;
-    const int64_t row = q0 + t * kTileM + r;
+    const int row = static_cast<int>(q0) + t * kTileM + r;
     const bool valid_row = row < p.nq;
     const int nbt = nb[t];
     const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
@@ -300,111 +355,151 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + row / kQueryGroup) : 0.0f;
     const float c_row = qs * p.scale_log2e;
     const float* kscale = p.kscale + bh * p.k_groups;
+    const float2 nb2 = make_float2(-kBias, -kBias);
 
-    float o[D];
+    float2 o[D / 2];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;
-    float pend_old = 0.0f, pend_w = 0.0f;  // weights of the PV block awaiting its fold
+    for (int i = 0; i < D / 2; ++i) o[i] = make_float2(0.0f, 0.0f);
+    // m_ref: reference max of the numerator and denominator (log2 units).
+    // It trails the true running max by less than kRescaleThreshold, which
+    // leaves o/l unchanged and skips almost every rescale.
+    float m_ref = -INFINITY, l_run = 0.0f;
+    float pend_w = 0.0f;  // weight of the PV block awaiting its fold
+    float bias_acc = 0.0f;  // o holds numerator + bias_acc (same FMAs with PV = 0)
     bool ok = true;
 
     for (int j = 0; j < nbt; ++j) {
       const int s = j % kStages;
       const int buf = j & 1;
-      if (!(ok = mbar_wait_warp(&kv_full[s], (j / kStages) & 1, budget, status, kStatusTimeoutFull, abort_flag)))
+      const float ks = __ldg(kscale + j);
+      if (!(ok = mbar_wait_warp(kv_full + 8 * (s), (j / kStages) & 1, budget, status, kStatusTimeoutFull, abort_flag)))
         break;
-      if (!(ok = mbar_wait_warp(&s_full[t * 2 + buf], (j >> 1) & 1, budget, status, kStatusTimeoutMma, abort_flag)))
+      if (!(ok = mbar_wait_warp(s_full + 8 * (t * 2 + buf), (j >> 1) & 1, budget, status, kStatusTimeoutMma, abort_flag)))
         break;
       tc_fence_after();
-      float x[kKeyBlock];
+      float2 x[kKeyBlock / 2];
       {
         uint32_t a[32], b[32];
-        tmem_ld32(tm_s + buf * kKeyBlock, a);
-        tmem_ld32(tm_s + buf * kKeyBlock + 32, b);
+        tmem_ld32_split(tm_s + buf * kKeyBlock, a);
+        tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
         tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[t * 2 + buf]);
-        const float c = c_row * __ldg(kscale + j);
-        const float4* vl = reinterpret_cast<const float4*>(smem + S::kOffVec + s * S::kVecBytes);
+        // Re-arm the S buffer; s_free is signalled after the P codes are out,
+        // by which time this store has long completed.
+        tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
+        const float c = c_row * ks;
+        const float2 c2 = make_float2(c, c);
+        const uint32_t vl = sbase + S::kOffVec + s * S::kVecBytes;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 la = vl[i], lb = vl[8 + i];
-          x[4 * i + 0] = fmaf(exact_i2f(a[4 * i + 0]), c, la.x);
-          x[4 * i + 1] = fmaf(exact_i2f(a[4 * i + 1]), c, la.y);
-          x[4 * i + 2] = fmaf(exact_i2f(a[4 * i + 2]), c, la.z);
-          x[4 * i + 3] = fmaf(exact_i2f(a[4 * i + 3]), c, la.w);
-          x[32 + 4 * i + 0] = fmaf(exact_i2f(b[4 * i + 0]), c, lb.x);
-          x[32 + 4 * i + 1] = fmaf(exact_i2f(b[4 * i + 1]), c, lb.y);
-          x[32 + 4 * i + 2] = fmaf(exact_i2f(b[4 * i + 2]), c, lb.z);
-          x[32 + 4 * i + 3] = fmaf(exact_i2f(b[4 * i + 3]), c, lb.w);
+          const float4 la = lds128(vl + 16 * i), lb = lds128(vl + 16 * (8 + i));
+          x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i], a[4 * i + 1]), nb2), c2, make_float2(la.x, la.y));
+          x[2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2], a[4 * i + 3]), nb2), c2, make_float2(la.z, la.w));
+          x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i], b[4 * i + 1]), nb2), c2, make_float2(lb.x, lb.y));
+          x[16 + 2 * i + 1] =
+              __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2], b[4 * i + 3]), nb2), c2, make_float2(lb.z, lb.w));
         }
       }
       if (p.causal) {
-        const int64_t key0 = static_cast<int64_t>(j) * kKeyBlock;
-        if (key0 + kKeyBlock - 1 > row) {
+        // Keys after this row are masked (reference.py:86-91); only the
+        // diagonal block needs work: lim = row - first key of the block.
+        const int lim = min(row - j * kKeyBlock, kKeyBlock);
+        if (lim < kKeyBlock - 1) {
 #pragma unroll
-          for (int i = 0; i < kKeyBlock; ++i)
-            if (key0 + i > row) x[i] = -INFINITY;
+          for (int i = 0; i < kKeyBlock / 2; ++i) {
+            if (2 * i > lim) x[i].x = -INFINITY;
+            if (2 * i + 1 > lim) x[i].y = -INFINITY;
+          }
         }
       }
-      float mb = x[0];
+      // Block max (reference.py:94-95), four independent 3-input chains.
+      float mx[4];
 #pragma unroll
-      for (int i = 1; i < kKeyBlock; ++i) mb = fmaxf(mb, x[i]);
-      const float m_new = fmaxf(m_run, mb);
+      for (int q = 0; q < 4; ++q) mx[q] = fmaxf(x[q].x, x[q].y);
+#pragma unroll
+      for (int i = 4; i < kKeyBlock / 2; i += 4) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) mx[q] = fmax3(mx[q], x[i + q].x, x[i + q].y);
+      }
+      const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+      // Lazy rescale of numerator and denominator (exact identity).
+      const bool need = mb > m_ref + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float new_ref = need ? mb : m_ref;
+        const float w_old = ex2_approx(m_ref - new_ref);
+        const float2 w2 = make_float2(w_old, w_old);
+#pragma unroll
+        for (int i = 0; i < D / 2; ++i) o[i] = __fmul2_rn(o[i], w2);
+        l_run *= w_old;
+        pend_w *= w_old;
+        bias_acc *= w_old;
+        m_ref = new_ref;
+      }
+      // Probabilities relative to the block max: e = p * vs in [0,1]
+      // (reference.py:99, 104-108); UINT8 codes round(255 e) half-to-even.
       const float m_use = (mb == -INFINITY) ? 0.0f : mb;
-      const float4* vr = reinterpret_cast<const float4*>(smem + S::kOffVec + s * S::kVecBytes) + kKeyBlock / 4;
-      float psum = 0.0f;
-      uint32_t words[kKeyBlock / 4];
+      const float2 mneg = make_float2(-m_use, -m_use);
+      const uint32_t vr = sbase + S::kOffVec + s * S::kVecBytes + kKeyBlock * 4;
+      float2 ps[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                      make_float2(0.0f, 0.0f)};
+      const float2 k255 = make_float2(255.0f, 255.0f);
+      const float2 kb2 = make_float2(kBias, kBias);
+      uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * kKeyBlock;
+      const int sw = (r >> 1) & 3;
 #pragma unroll
-      for (int w = 0; w < kKeyBlock / 4; ++w) {
-        const float4 rv = vr[w];
-        const float rr[4] = {rv.x, rv.y, rv.z, rv.w};
-        uint32_t y[4];
+      for (int c = 0; c < 4; ++c) {
+        uint32_t words[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float e = ex2_approx(x[4 * w + i] - m_use);
-          psum = fmaf(e, rr[i], psum);
-          y[i] = __float_as_uint(fmaf(e, 255.0f, 12582912.0f));
+        for (int q = 0; q < 4; ++q) {
+          const int w = 4 * c + q;
+          const float4 rv = lds128(vr + 16 * w);
+          float2 e0 = __fadd2_rn(x[2 * w], mneg);
+          float2 e1 = __fadd2_rn(x[2 * w + 1], mneg);
+          e0 = make_float2(ex2_approx(e0.x), ex2_approx(e0.y));
+          e1 = make_float2(ex2_approx(e1.x), ex2_approx(e1.y));
+          ps[q] = __ffma2_rn(e0, make_float2(rv.x, rv.y), ps[q]);
+          ps[q] = __ffma2_rn(e1, make_float2(rv.z, rv.w), ps[q]);
+          const float2 y0 = __ffma2_rn(e0, k255, kb2);
+          const float2 y1 = __ffma2_rn(e1, k255, kb2);
+          words[q] = __byte_perm(__byte_perm(__float_as_uint(y0.x), __float_as_uint(y0.y), 0x0040),
+                                 __byte_perm(__float_as_uint(y1.x), __float_as_uint(y1.y), 0x0040), 0x5410);
         }
-        words[w] = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
+        *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
       }
-      const float w_old = ex2_approx(m_run - m_new);
-      const float w_cur = ex2_approx(mb - m_new);
-      l_run = l_run * w_old + psum * w_cur;
-      m_run = m_new;
-      {
-        uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * kKeyBlock;
-        const int sw = (r >> 1) & 3;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) =
-              make_uint4(words[4 * c], words[4 * c + 1], words[4 * c + 2], words[4 * c + 3]);
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t * 2 + buf]);
+      fence_proxy_async_shared();
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(p_full + 8 * (t * 2 + buf));
+        mbar_arrive(s_free + 8 * (t * 2 + buf));
       }
-      if (j >= 1 && !(ok = fold_pv<D>(o, &pv_full[t], &pv_free[t], j - 1, tm_pv, pend_old, pend_w, lane, budget, status, abort_flag))) break;
-      pend_old = w_old;
+      const float psum = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
+      const float w_cur = (mb == -INFINITY) ? 0.0f : ex2_approx(mb - m_ref);
+      l_run = fmaf(psum, w_cur, l_run);
+      if (j >= 1 &&
+          !(ok = fold_pv<D>(o, pv_full + 8 * (t), pv_free + 8 * (t), j - 1, tm_pv, pend_w, lane, budget, status, abort_flag)))
+        break;
+      if (j >= 1) bias_acc = fmaf(kBias, pend_w, bias_acc);
       pend_w = w_cur * (1.0f / 255.0f);
     }
-    if (ok && nbt > 0) ok = fold_pv<D>(o, &pv_full[t], &pv_free[t], nbt - 1, tm_pv, pend_old, pend_w, lane, budget, status, abort_flag);
+    if (ok && nbt > 0)
+      ok = fold_pv<D>(o, pv_full + 8 * (t), pv_free + 8 * (t), nbt - 1, tm_pv, pend_w, lane, budget, status, abort_flag);
+    bias_acc = fmaf(kBias, pend_w, bias_acc);
 
-    if (ok && valid_row && !*abort_flag) {
+    if (ok && valid_row && flag_get(abort_flag) == 0) {
       const float inv = 1.0f / fmaxf(l_run, 1e-30f);
       const float* vm = p.vmean + bh * D;
-      uint32_t* orow = reinterpret_cast<uint32_t*>(static_cast<T*>(p.out) + (bh * p.nq + row) * D);
+      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq + row) * D);
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
+        const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);
+        const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c + 1);
         uint4 pk;
-        float f[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = o[c * 8 + i] * inv + __ldg(vm + c * 8 + i);
-        pk.x = pack2<T>(f[0], f[1]);
-        pk.y = pack2<T>(f[2], f[3]);
-        pk.z = pack2<T>(f[4], f[5]);
-        pk.w = pack2<T>(f[6], f[7]);
-        reinterpret_cast<uint4*>(orow)[c] = pk;
+        pk.x = pack2<T>(fmaf(o[4 * c].x - bias_acc, inv, m0.x), fmaf(o[4 * c].y - bias_acc, inv, m0.y));
+        pk.y = pack2<T>(fmaf(o[4 * c + 1].x - bias_acc, inv, m0.z), fmaf(o[4 * c + 1].y - bias_acc, inv, m0.w));
+        pk.z = pack2<T>(fmaf(o[4 * c + 2].x - bias_acc, inv, m1.x), fmaf(o[4 * c + 2].y - bias_acc, inv, m1.y));
+        pk.w = pack2<T>(fmaf(o[4 * c + 3].x - bias_acc, inv, m1.z), fmaf(o[4 * c + 3].y - bias_acc, inv, m1.w));
+        orow[c] = pk;
       }
     }
   }
@@ -433,8 +528,8 @@ __global__ void __launch_bounds__(128, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     ok_flag = 1;
-    mbar_init(&full_bar, 1);
-    mbar_init(&mma_bar, 1);
+    mbar_init(smem_u32(&full_bar), 1);
+    mbar_init(smem_u32(&mma_bar), 1);
     fence_mbarrier_init();
   }
   if (warp == 0) {
@@ -451,18 +546,18 @@ __global__ void __launch_bounds__(128, 1)
   for (int kb = 0; kb < slabs; ++kb) {
     if (threadIdx.x == 0 && ok_flag) {
       bool ok;
-      mbar_arrive_expect_tx(&full_bar, 128 * 128 + 64 * 128);
-      tma_load_3d(sa, &tmA, &full_bar, kb * 128, m0, 0);
-      tma_load_3d(sb, &tmB, &full_bar, kb * 128, n0, 0);
-      ok = mbar_wait(&full_bar, kb & 1, budget_ns, &g_piper_status, kStatusTimeoutFull, nullptr);
+      mbar_arrive_expect_tx(smem_u32(&full_bar), 128 * 128 + 64 * 128);
+      tma_load_3d(smem_u32(sa), &tmA, smem_u32(&full_bar), kb * 128, m0, 0);
+      tma_load_3d(smem_u32(sb), &tmB, smem_u32(&full_bar), kb * 128, n0, 0);
+      ok = mbar_wait(smem_u32(&full_bar), kb & 1, budget_ns, &g_piper_status, kStatusTimeoutFull, 0u);
       tc_fence_after();
       if (ok) {
         const uint64_t da = umma_desc_kmajor(smem_u32(sa), 128);
         const uint64_t db = umma_desc_kmajor(smem_u32(sb), 128);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) umma_i8(tmem, da + 2 * kk, db + 2 * kk, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&mma_bar);
-        ok = mbar_wait(&mma_bar, kb & 1, budget_ns, &g_piper_status, kStatusTimeoutMma, nullptr);
+        umma_commit(smem_u32(&mma_bar));
+        ok = mbar_wait(smem_u32(&mma_bar), kb & 1, budget_ns, &g_piper_status, kStatusTimeoutMma, 0u);
       }
       if (!ok) ok_flag = 0;
     }
@@ -491,12 +586,12 @@ __global__ void __launch_bounds__(128, 1)
 __global__ void selftest_wait_kernel(uint64_t budget_ns, int* timed_out, uint32_t* probe_status) {
   __shared__ uint64_t bar;
   if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(smem_u32(&bar), 1);
     fence_mbarrier_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const bool arrived = mbar_wait(&bar, 0, budget_ns, probe_status, kStatusTimeoutProbe, nullptr);
+    const bool arrived = mbar_wait(smem_u32(&bar), 0, budget_ns, probe_status, kStatusTimeoutProbe, 0u);
     *timed_out = arrived ? 0 : 1;
   }
 }

@@ -34,55 +34,67 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 }
 
 // ---------------------------------------------------------------- mbarrier
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+// Barriers and flags are addressed by 32-bit shared-window addresses
+// (smem_u32), which keeps them out of 64-bit generic registers.
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
 
 __device__ __forceinline__ void fence_mbarrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+               "r"(bytes)
                : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile(
-      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
-          smem_u32(bar)),
-      "r"(bytes)
-      : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// One probe of the phase; the thread may be suspended in hardware for up to
+// `hint_ns` while the phase is incomplete (it wakes as soon as it completes),
+// so waiting warps do not spin on the issue slots the working warps need.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t hint_ns = 0x100000u) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 
+// CTA-wide abort flag in shared memory (0 = keep going); address 0 = none.
+__device__ __forceinline__ uint32_t flag_get(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void flag_set(uint32_t addr, uint32_t v) {
+  asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // Waits until the phase with the given parity has completed.  Returns false
-// (after recording `status_bit` in *status) when `budget_ns` of wall-clock
-// time passes first.  *abort lets one failing warp stop the others quickly.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t budget_ns,
-                                          uint32_t* status, uint32_t status_bit,
-                                          volatile int* abort_flag) {
+// (after recording `status_bit` in *status and raising the abort flag) when
+// `budget_ns` of wall-clock time passes first, or as soon as another warp
+// has raised the abort flag.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t budget_ns, uint32_t* status,
+                                          uint32_t status_bit, uint32_t abort_addr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
-      if (abort_flag != nullptr && *abort_flag) return false;
+    if ((++spins & 3u) == 0) {
+      if (abort_addr != 0 && flag_get(abort_addr) != 0) return false;
       if (global_timer_ns() - start > budget_ns) {
         if (status != nullptr) atomicOr(status, status_bit);
-        if (abort_flag != nullptr) *abort_flag = 1;
+        if (abort_addr != 0) flag_set(abort_addr, 1u);
         return false;
       }
     }
@@ -92,10 +104,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 // Warp-uniform variant for code that synchronises the warp afterwards: every
 // lane waits (each bounded), then the warp agrees on success, so no lane can
 // leave a loop that its siblings stay in.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint64_t budget_ns,
-                                               uint32_t* status, uint32_t status_bit,
-                                               volatile int* abort_flag) {
-  const bool ok = mbar_wait(bar, parity, budget_ns, status, status_bit, abort_flag);
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, uint64_t budget_ns, uint32_t* status,
+                                               uint32_t status_bit, uint32_t abort_addr) {
+  const bool ok = mbar_wait(bar, parity, budget_ns, status, status_bit, abort_addr);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
@@ -112,22 +123,20 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 // 3-D tiled load into this CTA's shared memory; completion is signalled on
 // `bar` as transaction bytes.  The innermost coordinate c0 must be a multiple
 // of 16 bytes (all callers pass 0 or multiples of 64 bytes).
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
-                                            int c0, int c1, int c2) {
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
-                                          uint64_t* bar) {
+__device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* gmem_src, uint32_t bytes, uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(bar)
       : "memory");
 }
 
@@ -194,11 +203,8 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64
 
 // Arrives once on `bar` when every tcgen05.mma issued so far by this thread
 // has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ bool elect_one() {
@@ -227,12 +233,48 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// Same as tmem_ld32, issued as four .x8 loads: the destination of one load
+// must be a contiguous register block, and eight is far easier to place than
+// thirty-two when most registers already hold live state.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld32_split(uint32_t taddr, uint32_t (&r)[32]) {
+#ifdef PIPER_TMEM_LD4
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tmem_ld4(taddr + 4 * i, r + 4 * i);
+#else
+  tmem_ld8(taddr, r);
+  tmem_ld8(taddr + 8, r + 8);
+  tmem_ld8(taddr + 16, r + 16);
+  tmem_ld8(taddr + 24, r + 24);
+#endif
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Writes the same 32-bit value into 4 consecutive columns of this thread's lane.
+__device__ __forceinline__ void tmem_st4_same(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%1,%1,%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+
+// Writes the same 32-bit value into 8 consecutive columns of this thread's lane.
+__device__ __forceinline__ void tmem_st8_same(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+               : "memory");
 }
 
 // Writes the same 32-bit value into 16 consecutive columns of this thread's lane.
@@ -242,6 +284,15 @@ __device__ __forceinline__ void tmem_st16_same(uint32_t taddr, uint32_t v) {
       "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
       "r"(v)
       : "memory");
+}
+
+// 16-byte shared load the compiler keeps in program order relative to the
+// other volatile asm (it will not hoist a whole block of them ahead of the
+// TMEM waits, which would pin 64 extra registers).
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
 }
 
 // ---------------------------------------------------------------- math

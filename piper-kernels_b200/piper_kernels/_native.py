@@ -12,8 +12,12 @@ import ctypes
 import threading
 from pathlib import Path
 
+import os
+
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
-LIB_PATH = LIB_DIR / "libpiper_b200.so"
+# PIPER_B200_LIBRARY may point at another build of the same ABI (used to
+# compare kernel variants side by side); the default is the in-tree build.
+LIB_PATH = Path(os.environ.get("PIPER_B200_LIBRARY", LIB_DIR / "libpiper_b200.so"))
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1
