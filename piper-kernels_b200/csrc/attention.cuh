@@ -20,8 +20,9 @@
 //                    thread i owns row i = TMEM lane i; fp32 O in registers)
 //   warp 8           TMA producer: Q tiles once, then K, V^T tiles and the
 //                    per-key log2(vs), 1/vs vectors into a kStages ring
-//   warp 9           TMEM allocator + single-thread tcgen05.mma issuer:
-//                    QK^T of block j (both tiles) then PV of block j-1
+//   warp 9           TMEM allocator + single-thread tcgen05.mma issuer,
+//                    event driven: QK^T and PV of each tile issued as soon
+//                    as their operands and accumulators are ready
 // Shared-memory operands are in the canonical 128B/64B-swizzled K-major
 // layouts TMA writes; P codes are written by the softmax threads into the
 // same 64B-swizzled layout.  No multicast anywhere.
@@ -42,8 +43,17 @@ namespace piper {
 constexpr int kAttnThreads = 384;
 constexpr int kTileM = 128;  // query rows per softmax warpgroup
 constexpr int kTiles = 2;    // Q tiles per CTA
-constexpr int kStages = 4;   // K/V ring depth
+constexpr int kStages = 6;   // K/V ring depth
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s per wait
+// Register split (setmaxnreg): launch = 168 x 384 = 64512 registers; control
+// warpgroup 40, the two softmax warpgroups 232: 128*40 + 256*232 = 64512.
+// The host refuses to launch if the compiled kernel's launch register count
+// differs from kLaunchRegs, since an increase could then never be granted.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsControl = 40;
+constexpr int kRegsSoftmax = 232;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kLaunchRegs * kAttnThreads,
+              "setmaxnreg split exceeds the launch register allocation");
 
 __device__ uint32_t g_piper_status = 0;
 
@@ -249,7 +259,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
 
   if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     if (warp == 8 && lane == 0) {
       // ------------------------------------------------ TMA producer
       uint32_t q_bytes = 0;
@@ -283,58 +293,73 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_wait(q_full, 0, budget, status, kStatusTimeoutDrain, 0u);
     } else if (warp == 9 && lane == 0) {
       // ------------------------------------------------ MMA issuer
+      // Event driven: each tile advances on its own.  QK^T of block j needs
+      // the K/V stage loaded and the S buffer released by the softmax; PV of
+      // block j needs the P codes and the PV accumulator released by the
+      // previous fold.  Whatever is ready is issued; a stage is released to
+      // the producer once every tile has issued its PV for that block.
       constexpr uint32_t kIdescQK = umma_idesc_i8(true, true, kTileM, kKeyBlock);
       constexpr uint32_t kIdescPV = umma_idesc_i8(false, true, kTileM, D);
       bool ok = mbar_wait(q_full, 0, budget, status, kStatusTimeoutFull, abort_flag);
       tc_fence_after();
       uint64_t descQ[kTiles];
-      for (int t = 0; t < kTiles; ++t)
-        descQ[t] = umma_desc_kmajor(sbase + S::kOffQ + t * S::kQBytes, D);
-      for (int j = 0; ok && j <= nb_max; ++j) {
-        if (j < nb_max) {
-          const int s = j % kStages;
-          if (!(ok = mbar_wait(kv_full + 8 * (s), (j / kStages) & 1, budget, status, kStatusTimeoutFull, abort_flag)))
-            break;
-          tc_fence_after();
-          const uint64_t descK = umma_desc_kmajor(sbase + S::kOffK + s * S::kKBytes, D);
-          for (int t = 0; t < kTiles; ++t) {
-            if (j >= nb[t]) continue;
-            const int buf = j & 1;
-            if (!(ok = mbar_wait(s_free + 8 * (t * 2 + buf), ((j >> 1) & 1) ^ 1, budget, status,
-                                 kStatusTimeoutEmpty, abort_flag)))
-              break;
-            tc_fence_after();
-            const uint32_t dcol = tmem_base + t * 256 + buf * kKeyBlock;
+      for (int t = 0; t < kTiles; ++t) descQ[t] = umma_desc_kmajor(sbase + S::kOffQ + t * S::kQBytes, D);
+      const uint64_t descK0 = umma_desc_kmajor(sbase + S::kOffK, D);
+      const uint64_t descV0 = umma_desc_kmajor(sbase + S::kOffV, kKeyBlock);
+      const uint64_t descP0 = umma_desc_kmajor(sbase + S::kOffP, kKeyBlock);
+      int qk_next[kTiles] = {0, 0}, pv_next[kTiles] = {0, 0};
+      int released = 0;
+      uint64_t idle_since = 0;
+      while (ok) {
+        bool progress = false;
 #pragma unroll
-            for (int kk = 0; kk < D / 32; ++kk)
-              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, 1u);
-            umma_commit(s_full + 8 * (t * 2 + buf));
-          }
-          if (!ok) break;
-        }
-        if (j >= 1) {
-          const int jp = j - 1;
-          const int sp = jp % kStages;
-          const int bufp = jp & 1;
-          const uint64_t descV = umma_desc_kmajor(sbase + S::kOffV + sp * S::kVBytes, kKeyBlock);
-          for (int t = 0; t < kTiles; ++t) {
-            if (jp >= nb[t]) continue;
-            if (!(ok = mbar_wait(p_full + 8 * (t * 2 + bufp), (jp >> 1) & 1, budget, status, kStatusTimeoutFull,
-                                 abort_flag)))
-              break;
-            if (!(ok = mbar_wait(pv_free + 8 * (t), (jp & 1) ^ 1, budget, status, kStatusTimeoutEmpty, abort_flag)))
-              break;
+        for (int t = 0; t < kTiles; ++t) {
+          const int jq = qk_next[t];
+          if (jq < nb[t] && mbar_test(kv_full + 8 * (jq % kStages), (jq / kStages) & 1) &&
+              mbar_test(s_free + 8 * (t * 2 + (jq & 1)), ((jq >> 1) & 1) ^ 1)) {
             tc_fence_after();
-            const uint64_t descP =
-                umma_desc_kmajor(sbase + S::kOffP + (t * 2 + bufp) * S::kPBytes, kKeyBlock);
+            const uint64_t descK = descK0 + static_cast<uint64_t>(((jq % kStages) * S::kKBytes) >> 4);
+            const uint32_t dcol = tmem_base + t * 256 + (jq & 1) * kKeyBlock;
+#pragma unroll
+            for (int kk = 0; kk < D / 32; ++kk) umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, 1u);
+            umma_commit(s_full + 8 * (t * 2 + (jq & 1)));
+            qk_next[t] = jq + 1;
+            progress = true;
+          }
+          const int jp = pv_next[t];
+          if (jp < qk_next[t] && mbar_test(p_full + 8 * (t * 2 + (jp & 1)), (jp >> 1) & 1) &&
+              mbar_test(pv_free + 8 * t, (jp & 1) ^ 1)) {
+            tc_fence_after();
+            const uint64_t descV = descV0 + static_cast<uint64_t>(((jp % kStages) * S::kVBytes) >> 4);
+            const uint64_t descP = descP0 + static_cast<uint64_t>(((t * 2 + (jp & 1)) * S::kPBytes) >> 4);
             const uint32_t dcol = tmem_base + t * 256 + 128;
 #pragma unroll
-            for (int kk = 0; kk < kKeyBlock / 32; ++kk)
-              umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, 1u);
-            umma_commit(pv_full + 8 * (t));
+            for (int kk = 0; kk < kKeyBlock / 32; ++kk) umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, 1u);
+            umma_commit(pv_full + 8 * t);
+            pv_next[t] = jp + 1;
+            progress = true;
           }
-          if (!ok) break;
-          umma_commit(kv_empty + 8 * (sp));
+        }
+        while (released < nb_max && (released >= nb[0] || pv_next[0] > released) &&
+               (released >= nb[1] || pv_next[1] > released)) {
+          umma_commit(kv_empty + 8 * (released % kStages));
+          ++released;
+        }
+        if (released >= nb_max) break;
+        if (progress) {
+          idle_since = 0;
+        } else {
+          const uint64_t now = global_timer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > budget) {
+            atomicOr(status, kStatusTimeoutEmpty);
+            flag_set(abort_flag, 1u);
+            ok = false;
+          } else if (flag_get(abort_flag) != 0) {
+            ok = false;
+          }
+          __nanosleep(32);
         }
       }
       // Everything issued must complete before TMEM is freed.
@@ -342,7 +367,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_wait(mma_done, 0, budget, status, kStatusTimeoutMma, 0u);
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 232;");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // -------------------------------------------------- softmax warpgroups
     const int t = warp / 4;
     const int r = threadIdx.x % kTileM;
@@ -421,6 +446,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int q = 0; q < 4; ++q) mx[q] = fmax3(mx[q], x[i + q].x, x[i + q].y);
       }
       const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+      // The S buffer was re-armed right after it was read; release it now (the
+      // store has completed behind the max) so QK^T two blocks ahead can start.
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free + 8 * (t * 2 + buf));
       // Lazy rescale of numerator and denominator (exact identity).
       const bool need = mb > m_ref + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
@@ -466,13 +497,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
       }
       fence_proxy_async_shared();
-      tmem_st_wait();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(p_full + 8 * (t * 2 + buf));
-        mbar_arrive(s_free + 8 * (t * 2 + buf));
-      }
+      if (lane == 0) mbar_arrive(p_full + 8 * (t * 2 + buf));
       const float psum = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
       const float w_cur = (mb == -INFINITY) ? 0.0f : ex2_approx(mb - m_ref);
       l_run = fmaf(psum, w_cur, l_run);

@@ -69,14 +69,24 @@ int ensure_device(int* device_out) {
       return fail(PIPER_B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     g_encode = reinterpret_cast<EncodeTiledFn>(fn);
   }
-  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__half, 64>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<64>::kAlloc));
-  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__half, 128>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<128>::kAlloc));
-  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__nv_bfloat16, 64>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<64>::kAlloc));
-  PIPER_CUDA(cudaFuncSetAttribute(piper::piper_attention_kernel<__nv_bfloat16, 128>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, piper::AttnSmem<128>::kAlloc));
+  // The attention kernels redistribute registers between warpgroups with
+  // setmaxnreg, which is only safe at the launch register count the split was
+  // computed for.
+  const void* kernels[4] = {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>)};
+  const int smem_bytes[4] = {piper::AttnSmem<64>::kAlloc, piper::AttnSmem<128>::kAlloc, piper::AttnSmem<64>::kAlloc,
+                             piper::AttnSmem<128>::kAlloc};
+  for (int i = 0; i < 4; ++i) {
+    PIPER_CUDA(cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes[i]));
+    cudaFuncAttributes attr;
+    PIPER_CUDA(cudaFuncGetAttributes(&attr, kernels[i]));
+    if (attr.numRegs != piper::kLaunchRegs)
+      return fail(PIPER_B200_ERR_CUDA, "attention kernel compiled with " + std::to_string(attr.numRegs) +
+                                           " registers per thread; its warpgroup register split needs " +
+                                           std::to_string(piper::kLaunchRegs));
+  }
   g_device_ready[device] = true;
   return PIPER_B200_OK;
 }
