@@ -44,7 +44,8 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
 }
 
-// Loads 8 consecutive elements (16 bytes when `kVec16`, else element-wise).
+// Loads 8 consecutive elements as floats (16 bytes when `kVec16`, else
+// element-wise).
 template <typename T, bool kVec16>
 __device__ __forceinline__ void load8(const T* p, float (&out)[8]) {
   if constexpr (kVec16) {
@@ -58,10 +59,22 @@ __device__ __forceinline__ void load8(const T* p, float (&out)[8]) {
   }
 }
 
-__device__ __forceinline__ int8_t quantize_int8(float x, float scale) {
-  float r = rintf(__fdiv_rn(x, scale));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
+// clamp(round_half_even(x / scale), -127, 127), bit-exact with the IEEE
+// quotient, without a division or a float-to-int conversion per element.
+// q = x * (1/scale) (reciprocal correctly rounded) is within
+// |x/scale| * 2^-22 <= 127 * 2^-22 < 2^-14 of the true quotient
+// (|x| <= amax < 127 * scale), so rounding q gives the same integer unless q
+// lies within 2^-14 of a half-integer; only then is the exact quotient used.
+// Rounding is the add of 1.5 * 2^23 (half-to-even in the FPU), and clamping
+// before rounding equals clamping after it because the bounds are integers.
+// Returns the float bits of 1.5 * 2^23 + code: the low byte is the INT8 code.
+__device__ __forceinline__ uint32_t quantize_bits(float x, float scale, float rcp) {
+  constexpr float kMagic = 12582912.0f;
+  const float q = fminf(fmaxf(__fmul_rn(x, rcp), -127.0f), 127.0f);
+  float y = __fadd_rn(q, kMagic);
+  if (fabsf(__fsub_rn(q, __fsub_rn(y, kMagic))) > 0.5f - 1.0f / 16384.0f)
+    y = __fadd_rn(fminf(fmaxf(__fdiv_rn(x, scale), -127.0f), 127.0f), kMagic);
+  return __float_as_uint(y);
 }
 
 __device__ __forceinline__ float group_scale(float amax) {
@@ -160,129 +173,167 @@ __global__ void __launch_bounds__(kPrepassThreads) kv_sum_kernel(PrepassArgs a) 
 }
 
 // ---------------------------------------------------------------------------
-// Block-wide max of non-negative values; `scratch` holds one float per warp.
-__device__ __forceinline__ float block_max_nonneg(float v, float* scratch) {
+// Raw 16-byte load of 8 consecutive fp16/bf16 elements (element-wise when the
+// address or strides are not 16-byte aligned) and its exact widening.
+template <typename T, bool kVec16>
+__device__ __forceinline__ uint4 load_raw8(const T* p) {
+  if constexpr (kVec16) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+  } else {
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(p);
+    uint32_t w[4];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  __syncthreads();
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  float m = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kPrepassThreads / 32; ++w) m = fmaxf(m, scratch[w]);
-  return m;
+    for (int i = 0; i < 4; ++i) w[i] = static_cast<uint32_t>(e[2 * i]) | (static_cast<uint32_t>(e[2 * i + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
 }
 
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& r, float (&out)[8]) {
+  const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = to_f32<T>(e[i]);
+}
+
+// Eight INT8 codes packed into two words (low byte of each code's bits).
+__device__ __forceinline__ uint2 pack_codes(const float (&x)[8], float s, float rs) {
+  uint32_t y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) y[i] = quantize_bits(x[i], s, rs);
+  const uint32_t w0 = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
+  const uint32_t w1 = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);
+  return make_uint2(w0, w1);
+}
+
+// One 64-row tile of Q, K and V per CTA.  All loads are issued up front; the
+// two 32-row Q group maxima and the 64-row K group max share one block-wide
+// reduction; each V row's max is a shuffle among the threads of that row.  V
+// codes go row-major into a padded shared tile (row stride D/4+1 words, so
+// rows fall on distinct banks), then are transposed 4x4 bytes at a time with
+// byte permutes and written as [D, keys] with coalesced 4-byte stores.
 template <typename T, int D, bool kVec16>
 __global__ void __launch_bounds__(kPrepassThreads) quantize_kernel(PrepassArgs a) {
-  constexpr int kVpr = D / 8;
-  constexpr int kRpp = kPrepassThreads / kVpr;
-  constexpr int kPasses = kKeyBlock / kRpp;  // 64-row tile
-  __shared__ float scratch[2][kPrepassThreads / 32];
-  __shared__ __align__(16) int8_t vt[D][kKeyBlock];
+  constexpr int kVpr = D / 8;                   // 16-byte vectors per row
+  constexpr int kRpp = kPrepassThreads / kVpr;  // rows per pass
+  constexpr int kPasses = kKeyBlock / kRpp;     // passes over the 64-row tile
+  constexpr int kRowWords = D / 4 + 1;          // padded V code row, in words
+  constexpr int kWarps = kPrepassThreads / 32;
+  __shared__ float red[kWarps][3];
+  __shared__ uint32_t vrow[kKeyBlock * kRowWords];
 
   const int tile = blockIdx.x;
   const int64_t bh = blockIdx.y;
   const int64_t b = bh / a.heads, h = bh % a.heads;
   const int tid = threadIdx.x;
+  const int lane = tid % 32, warp = tid / 32;
   const int vec = tid % kVpr;
   const int ro = tid / kVpr;
   const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
   const auto& L = a.L;
+  const bool has_q = row0 < a.nq;
+  const bool has_kv = row0 < a.nk;
 
-  // ---- Q: two 32-row groups per tile.
-  if (row0 < a.nq) {
-    const T* base = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + vec * 8;
-    float x[kPasses][8];
-    float amax[2] = {0.0f, 0.0f};
+  const T* qb = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + vec * 8;
+  const T* kb = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + vec * 8;
+  const T* vb = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + vec * 8;
+  uint4 rq[kPasses], rk[kPasses], rv[kPasses];
 #pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      const int lr = ro + p * kRpp;
-      const int64_t r = row0 + lr;
-      if (r < a.nq) {
-        load8<T, kVec16>(base + r * a.qs[2], x[p]);
-      } else {
+  for (int p = 0; p < kPasses; ++p) {
+    const int64_t r = row0 + ro + p * kRpp;
+    rq[p] = (r < a.nq) ? load_raw8<T, kVec16>(qb + r * a.qs[2]) : make_uint4(0u, 0u, 0u, 0u);
+    const bool kv_ok = r < a.nk;
+    rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + r * a.ks[2]) : make_uint4(0u, 0u, 0u, 0u);
+    rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + r * a.vs[2]) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float km[8], vm[8];
+  {
+    const float* kmean = reinterpret_cast<const float*>(a.ws + L.kmean) + bh * D + vec * 8;
+    const float* vmean = reinterpret_cast<const float*>(a.ws + L.vmean) + bh * D + vec * 8;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) x[p][i] = 0.0f;
-      }
-      const int g = (p * kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax[g] = fmaxf(amax[g], fabsf(x[p][i]));
+    for (int i = 0; i < 8; ++i) {
+      km[i] = has_kv ? kmean[i] : 0.0f;
+      vm[i] = (has_kv && !a.causal) ? vmean[i] : 0.0f;
     }
-    float scale[2];
-    scale[0] = group_scale(block_max_nonneg(amax[0], scratch[0]));
-    scale[1] = group_scale(block_max_nonneg(amax[1], scratch[1]));
+  }
+
+  // ---- group maxima: Q (two 32-row groups) and centered K (one 64-row group);
+  // rows past the sequence end count as zero, as the reference's zero padding.
+  float am[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int p = 0; p < kPasses; ++p) {
+    const int64_t r = row0 + ro + p * kRpp;
+    float x[8];
+    unpack8<T>(rq[p], x);
+    const int g = (p * kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am[g] = fmaxf(am[g], fabsf(x[i]));
+    if (r < a.nk) {
+      unpack8<T>(rk[p], x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) am[2] = fmaxf(am[2], fabsf(__fsub_rn(x[i], km[i])));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) am[c] = fmaxf(am[c], __shfl_xor_sync(0xffffffffu, am[c], o));
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) red[warp][c] = am[c];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    float m = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[w][c]);
+    am[c] = m;
+  }
+
+  // ---- Q codes.
+  if (has_q) {
+    const float sq[2] = {group_scale(am[0]), group_scale(am[1])};
+    const float rq2[2] = {__frcp_rn(sq[0]), __frcp_rn(sq[1])};
     int8_t* q8 = reinterpret_cast<int8_t*>(a.ws + L.q8);
-    float* qscale = reinterpret_cast<float*>(a.ws + L.qscale);
     if (tid < 2) {
       const int64_t g = row0 / kQueryGroup + tid;
-      if (g < L.q_groups) qscale[bh * L.q_groups + g] = scale[tid];
+      if (g < L.q_groups) reinterpret_cast<float*>(a.ws + L.qscale)[bh * L.q_groups + g] = sq[tid];
     }
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int lr = ro + p * kRpp;
-      const int64_t r = row0 + lr;
+      const int64_t r = row0 + ro + p * kRpp;
       if (r < a.nq) {
-        const float s = scale[(p * kRpp) / kQueryGroup];
-        uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          packed[i / 4] |= (static_cast<uint32_t>(static_cast<uint8_t>(quantize_int8(x[p][i], s))))
-                           << (8 * (i % 4));
-        *reinterpret_cast<uint2*>(q8 + (bh * a.nq + r) * D + vec * 8) = make_uint2(packed[0], packed[1]);
+        const int g = (p * kRpp) / kQueryGroup;
+        float x[8];
+        unpack8<T>(rq[p], x);
+        *reinterpret_cast<uint2*>(q8 + (bh * a.nq + r) * D + vec * 8) = pack_codes(x, sq[g], rq2[g]);
       }
     }
   }
+  if (!has_kv) return;
 
-  if (row0 >= a.nk) return;
-  const float* kmean = reinterpret_cast<const float*>(a.ws + L.kmean) + bh * D + vec * 8;
-  const float* vmean = reinterpret_cast<const float*>(a.ws + L.vmean) + bh * D + vec * 8;
-
-  // ---- K: centered by the sequence mean, one 64-row group per tile.
+  // ---- K codes (centered by the sequence mean).
   {
-    const T* base = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + vec * 8;
-    float m[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m[i] = kmean[i];
-    float x[kPasses][8];
-    float amax = 0.0f;
-#pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      const int64_t r = row0 + ro + p * kRpp;
-      if (r < a.nk) {
-        load8<T, kVec16>(base + r * a.ks[2], x[p]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          x[p][i] = __fsub_rn(x[p][i], m[i]);
-          amax = fmaxf(amax, fabsf(x[p][i]));
-        }
-      }
-    }
-    const float s = group_scale(block_max_nonneg(amax, scratch[0]));
+    const float sk = group_scale(am[2]);
+    const float rsk = __frcp_rn(sk);
     int8_t* k8 = reinterpret_cast<int8_t*>(a.ws + L.k8);
-    float* kscale = reinterpret_cast<float*>(a.ws + L.kscale);
-    if (tid == 0) kscale[bh * L.k_groups + tile] = s;
+    if (tid == 0) reinterpret_cast<float*>(a.ws + L.kscale)[bh * L.k_groups + tile] = sk;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
       const int64_t r = row0 + ro + p * kRpp;
       if (r < a.nk) {
-        uint32_t packed[2] = {0u, 0u};
+        float x[8];
+        unpack8<T>(rk[p], x);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          packed[i / 4] |= (static_cast<uint32_t>(static_cast<uint8_t>(quantize_int8(x[p][i], s))))
-                           << (8 * (i % 4));
-        *reinterpret_cast<uint2*>(k8 + (bh * a.nk + r) * D + vec * 8) = make_uint2(packed[0], packed[1]);
+        for (int i = 0; i < 8; ++i) x[i] = __fsub_rn(x[i], km[i]);
+        *reinterpret_cast<uint2*>(k8 + (bh * a.nk + r) * D + vec * 8) = pack_codes(x, sk, rsk);
       }
     }
   }
 
-  // ---- V: per key row, centered when non-causal; codes transposed.
+  // ---- V: per key row (centered when non-causal), codes into the shared tile.
   {
-    const T* base = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + vec * 8;
-    float m[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m[i] = a.causal ? 0.0f : vmean[i];
     float* vscale = reinterpret_cast<float*>(a.ws + L.vscale) + bh * L.nk_pad;
     float* vlog2 = reinterpret_cast<float*>(a.ws + L.vlog2) + bh * L.nk_pad;
     float* vrcp = reinterpret_cast<float*>(a.ws + L.vrcp) + bh * L.nk_pad;
@@ -292,38 +343,50 @@ __global__ void __launch_bounds__(kPrepassThreads) quantize_kernel(PrepassArgs a
       const int64_t r = row0 + lr;
       const bool valid = r < a.nk;
       float x[8];
+      unpack8<T>(rv[p], x);
       float amax = 0.0f;
-      if (valid) {
-        load8<T, kVec16>(base + r * a.vs[2], x);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          x[i] = __fsub_rn(x[i], m[i]);
-          amax = fmaxf(amax, fabsf(x[i]));
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = 0.0f;
+      for (int i = 0; i < 8; ++i) {
+        x[i] = __fsub_rn(x[i], vm[i]);
+        amax = fmaxf(amax, fabsf(x[i]));
       }
+      if (!valid) amax = 0.0f;
       // The kVpr threads of one row are consecutive lanes.
 #pragma unroll
       for (int o = kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float s = group_scale(amax);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) vt[vec * 8 + i][lr] = valid ? quantize_int8(x[i], s) : int8_t(0);
+      const float rs = __frcp_rn(s);
+      const uint2 codes = valid ? pack_codes(x, s, rs) : make_uint2(0u, 0u);
+      vrow[lr * kRowWords + 2 * vec] = codes.x;
+      vrow[lr * kRowWords + 2 * vec + 1] = codes.y;
       if (vec == 0) {
         vscale[r] = valid ? s : 0.0f;
         vlog2[r] = valid ? log2f(s) : -INFINITY;
-        vrcp[r] = valid ? __frcp_rn(s) : 0.0f;
+        vrcp[r] = valid ? rs : 0.0f;
       }
     }
-    __syncthreads();
-    int8_t* v8t = reinterpret_cast<int8_t*>(a.ws + L.v8t);
-    constexpr int kChunks = D * kKeyBlock / 16;  // 16-byte pieces of the [D][64] tile
-    for (int c = tid; c < kChunks; c += kPrepassThreads) {
-      const int d = c / (kKeyBlock / 16);
-      const int part = c % (kKeyBlock / 16);
-      *reinterpret_cast<int4*>(v8t + (bh * D + d) * L.nk_pad + row0 + part * 16) =
-          *reinterpret_cast<const int4*>(&vt[d][part * 16]);
+  }
+  __syncthreads();
+  // ---- transpose to [D, keys]: each step moves a 4-key x 4-feature block.
+  {
+    uint32_t* v8t = reinterpret_cast<uint32_t*>(a.ws + L.v8t);
+    constexpr int kBlocks = (D / 4) * (kKeyBlock / 4);
+#pragma unroll
+    for (int blk = tid; blk < kBlocks; blk += kPrepassThreads) {
+      const int kq = blk % (kKeyBlock / 4);
+      const int dq = blk / (kKeyBlock / 4);
+      const uint32_t w0 = vrow[(4 * kq + 0) * kRowWords + dq];
+      const uint32_t w1 = vrow[(4 * kq + 1) * kRowWords + dq];
+      const uint32_t w2 = vrow[(4 * kq + 2) * kRowWords + dq];
+      const uint32_t w3 = vrow[(4 * kq + 3) * kRowWords + dq];
+      const uint32_t t0 = __byte_perm(w0, w1, 0x5140), t1 = __byte_perm(w2, w3, 0x5140);
+      const uint32_t t2 = __byte_perm(w0, w1, 0x7362), t3 = __byte_perm(w2, w3, 0x7362);
+      const uint32_t o[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632), __byte_perm(t2, t3, 0x5410),
+                             __byte_perm(t2, t3, 0x7632)};
+      // word index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and row0 are multiples of 64.
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v8t[((bh * D + 4 * dq + j) * L.nk_pad + row0) / 4 + kq] = o[j];
     }
   }
 }

@@ -80,6 +80,28 @@ def test_prepass_matches_oracle_on_random_shapes(dtype, head_dim, is_causal, n) 
     _check_against_oracle(q, k, v, is_causal)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("amax", [1.0, 3.75, 127.0])
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_prepass_rounding_over_every_representable_input(dtype, amax, is_causal) -> None:
+    # Every finite value of the input type in [-amax, amax] is quantized, each
+    # 32x128 block holding amax once so the query scale is fixed: every
+    # quotient's rounding (near-ties included) is checked against the
+    # oracle's IEEE division, for Q, K and V codes alike.
+    patterns = torch.arange(-(1 << 15), 1 << 15, dtype=torch.int32).to(torch.int16).view(dtype)
+    values = patterns[torch.isfinite(patterns) & (patterns.float().abs() <= amax)]
+    per_block = 32 * 128 - 1
+    blocks = -(-values.numel() // per_block)
+    flat = torch.zeros(blocks * per_block, dtype=dtype)
+    flat[: values.numel()] = values
+    flat = flat.reshape(blocks, per_block)
+    head = torch.full((blocks, 1), amax, dtype=dtype)
+    q = torch.cat([head, flat], dim=1).reshape(1, 1, blocks * 32, 128)
+    k = q.flip(2).contiguous()
+    v = q.roll(17, dims=3).contiguous()
+    _check_against_oracle(q, k, v, is_causal)
+
+
 def test_prepass_rectangular_and_strided_inputs() -> None:
     dev = require_b200()
     g = torch.Generator().manual_seed(5)
