@@ -64,6 +64,10 @@ typedef struct piper_b200_workspace_layout_s {
   uint64_t q8, k8, v8t, qscale, kscale, vscale, vlog2, vrcp, kmean, vmean, ksum, vsum, counter;
   uint64_t total_bytes;
   int64_t q_groups, k_groups, nk_pad, chunks;
+  /* k8 .. vrcp form one contiguous span: [kv_pack, kv_pack + kv_pack_bytes). */
+  uint64_t kv_pack, kv_pack_bytes;
+  /* fp64 [2, B*H, D]: K then V column sums of a sequence shard. */
+  uint64_t totals;
 } piper_b200_workspace_layout_t;
 
 /* ABI version of this header (major*100 + minor). */
@@ -104,6 +108,53 @@ int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], 
                              int64_t heads, int64_t query_length, int64_t key_length,
                              int64_t head_dim, double scale, int is_causal, void* workspace,
                              size_t workspace_bytes, void* stream);
+
+/* ---- Sequence-sharded (ring) attention --------------------------------
+ * For a sequence split over ranks (rank r holds query/key/value rows of
+ * shard r).  No counterpart in the reference, which runs on one GPU; these
+ * three calls compose the same arithmetic as piper_b200_attention_fwd:
+ *   1. piper_b200_shard_column_sums: the shard's fp64 K (and V) column sums
+ *      into the workspace's `totals` region (fp64 [2, B*H, D]).
+ *   2. The caller sums `totals` over the ranks (e.g. an NCCL all-reduce),
+ *      then piper_b200_shard_prepass turns them into the sequence means
+ *      (divided by total_keys) and quantizes this shard.  Shards must start at
+ *      multiples of 64 rows so the per-64-row K groups match one GPU's.
+ *   3. piper_b200_attention_shard once per key shard, the K/V operands taken
+ *      from a K/V pack (the workspace's span [kv_pack, kv_pack+kv_pack_bytes)
+ *      of the rank that owns the keys, copied here), carrying each query row's
+ *      online-softmax state in `state` (piper_b200_state_bytes) between calls:
+ *      state_mode PIPER_B200_STATE_LOAD continues from the state, and
+ *      PIPER_B200_STATE_STORE writes the state instead of the output, so the
+ *      last call omits STORE and writes `out`.  For causal attention,
+ *      causal_shift = first query position - first key position of the two
+ *      shards (keys with local index > query local index + shift are masked). */
+#define PIPER_B200_STATE_LOAD 1
+#define PIPER_B200_STATE_STORE 2
+
+int piper_b200_shard_column_sums(const void* key, const int64_t key_strides[3], const void* value,
+                                 const int64_t value_strides[3], int dtype, int64_t batch,
+                                 int64_t heads, int64_t query_length, int64_t key_length,
+                                 int64_t head_dim, int is_causal, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+int piper_b200_shard_prepass(const void* query, const int64_t query_strides[3], const void* key,
+                             const int64_t key_strides[3], const void* value,
+                             const int64_t value_strides[3], int dtype, int64_t batch,
+                             int64_t heads, int64_t query_length, int64_t key_length,
+                             int64_t head_dim, int is_causal, int64_t total_keys, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+int piper_b200_attention_shard(void* out, int dtype, int64_t batch, int64_t heads,
+                               int64_t query_length, int64_t key_length, int64_t head_dim,
+                               double scale, int is_causal, int64_t causal_shift,
+                               const void* workspace, size_t workspace_bytes, const void* kv_pack,
+                               float* state, int state_mode, void* stream);
+
+/* Bytes of the per-row state of piper_b200_attention_shard: fp32
+ * [B*H, Nq, D] numerators followed by fp32 [B*H, Nq, 2] (max, denominator);
+ * 0 for non-positive sizes. */
+size_t piper_b200_state_bytes(int64_t batch, int64_t heads, int64_t query_length,
+                              int64_t head_dim);
 
 /* Scratch capacity of piper_b200_attention_fwd_no_alloc: 16 MiB per GPU. */
 #define PIPER_B200_NO_ALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)

@@ -74,6 +74,12 @@ def _load() -> ctypes.CDLL:
             i64, i64, i64, i64, ctypes.c_float, ctypes.c_int, _F32P,
         ]
         lib.pk_attention.restype = None
+        lib.pk_attention_shard.argtypes = [
+            _I8P, _F32P, _I8P, _F32P, _I8P, _F32P, ctypes.c_void_p,
+            i64, i64, i64, i64, ctypes.c_float, ctypes.c_int, i64,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+        ]
+        lib.pk_attention_shard.restype = None
         _lib = lib
     return _lib
 
@@ -173,6 +179,37 @@ def attention_prepared(p: Prepared, scale: float, is_causal: bool) -> np.ndarray
         p.query_int8, p.query_scale, p.key_int8, p.key_scale, p.value_int8,
         p.value_scale, _ptr(vm), b * h, nq, nk, d, ctypes.c_float(scale),
         1 if is_causal else 0, out,
+    )
+    return out
+
+
+STATE_LOAD = 1
+STATE_STORE = 2
+
+
+def attention_shard(query_side: Prepared, key_side: Prepared, scale: float, is_causal: bool, *,
+                    causal_shift: int = 0, state: tuple[np.ndarray, np.ndarray] | None = None,
+                    state_mode: int = 0) -> np.ndarray | None:
+    """The recurrence over one key shard (pk_attention_shard).
+
+    Q codes/scales and the V mean come from ``query_side``; K/V codes and
+    scales from ``key_side``.  ``state`` = (numerator f32 [B,H,Nq,D],
+    (max, denominator) f32 [B,H,Nq,2]) is read with STATE_LOAD and written with
+    STATE_STORE; without STATE_STORE the fp32 output is returned.
+    """
+    b, h, nq, d = query_side.query_int8.shape
+    nk = key_side.key_int8.shape[2]
+    out = None if state_mode & STATE_STORE else np.empty((b, h, nq, d), np.float32)
+    so, sml = state if state is not None else (None, None)
+    for arr, shape in ((so, (b, h, nq, d)), (sml, (b, h, nq, 2))):
+        if state_mode and (arr is None or arr.dtype != np.float32 or arr.shape != shape
+                           or not arr.flags.c_contiguous):
+            raise ValueError("state arrays must be contiguous float32 of the query shard's shape")
+    vm = None if query_side.value_mean is None else np.ascontiguousarray(query_side.value_mean, np.float32)
+    _load().pk_attention_shard(
+        query_side.query_int8, query_side.query_scale, key_side.key_int8, key_side.key_scale,
+        key_side.value_int8, key_side.value_scale, _ptr(vm), b * h, nq, nk, d, ctypes.c_float(scale),
+        1 if is_causal else 0, int(causal_shift), _ptr(so), _ptr(sml), int(state_mode), _ptr(out),
     )
     return out
 

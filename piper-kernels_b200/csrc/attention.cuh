@@ -27,6 +27,12 @@
 // layouts TMA writes; P codes are written by the softmax threads into the
 // same 64B-swizzled layout.  No multicast anywhere.
 //
+// Sequence shards (ring attention): the recurrence above is associative over
+// key blocks, so a launch may cover one shard of the keys and carry each
+// row's (O, m, l) in a state buffer to the launch over the next shard
+// (state_mode); only the last launch writes the output.  causal_shift places
+// the key shard relative to the query shard for the causal mask.
+//
 // Every mbarrier wait is bounded (sm100.cuh): on timeout the CTA raises an
 // abort flag, all roles leave their loops, drain what they issued (bounded),
 // free TMEM and exit; the host reads the status word.
@@ -88,7 +94,19 @@ struct AttnParams {
   int causal;
   int q_tiles;  // ceil(Nq / 256)
   uint64_t wait_budget_ns;
+  // Sequence shards.  Causal visibility is key <= query + causal_shift in
+  // shard-local indices (causal_shift = first query position - first key
+  // position; 0 for one shard).  state_mode: kStateLoad starts every row from
+  // the carried (numerator, reference max, denominator) instead of zero;
+  // kStateStore writes that triple back instead of the output.
+  int64_t causal_shift;
+  int state_mode;
+  float* state_o;   // f32 [B*H, Nq, D]  numerator (bias-free)
+  float* state_ml;  // f32 [B*H, Nq, 2]  (reference max in log2 units, denominator)
 };
+
+constexpr int kStateLoad = 1;
+constexpr int kStateStore = 2;
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -204,8 +222,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (first >= p.nq) {
       nb[t] = 0;
     } else if (p.causal) {
-      const int64_t last = min(first + kTileM - 1, p.nq - 1);
-      nb[t] = min(static_cast<int>(last / kKeyBlock) + 1, nblocks_all);
+      // Last key any row of the tile sees; none when the whole shard of keys
+      // lies after the tile.
+      const int64_t last_key = min(first + kTileM - 1, p.nq - 1) + p.causal_shift;
+      nb[t] = last_key < 0 ? 0 : static_cast<int>(min(last_key / kKeyBlock + 1, static_cast<int64_t>(nblocks_all)));
     } else {
       nb[t] = nblocks_all;
     }
@@ -392,6 +412,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float pend_w = 0.0f;  // weight of the PV block awaiting its fold
     float bias_acc = 0.0f;  // o holds numerator + bias_acc (same FMAs with PV = 0)
     bool ok = true;
+    if ((p.state_mode & kStateLoad) && valid_row) {
+      // Continue the recurrence of earlier key shards: the same identity as
+      // a lazy rescale, with the carried reference max.
+      const float4* so = reinterpret_cast<const float4*>(p.state_o + (bh * p.nq + row) * D);
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i) {
+        const float4 v = so[i];
+        o[2 * i] = make_float2(v.x, v.y);
+        o[2 * i + 1] = make_float2(v.z, v.w);
+      }
+      const float2 ml = reinterpret_cast<const float2*>(p.state_ml)[bh * p.nq + row];
+      m_ref = ml.x;
+      l_run = ml.y;
+    }
 
     for (int j = 0; j < nbt; ++j) {
       const int s = j % kStages;
@@ -426,8 +460,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       if (p.causal) {
         // Keys after this row are masked (reference.py:86-91); only the
-        // diagonal block needs work: lim = row - first key of the block.
-        const int lim = min(row - j * kKeyBlock, kKeyBlock);
+        // diagonal block needs work: lim = last visible key - first key of
+        // the block, clamped to [-1, 64].
+        const int lim = static_cast<int>(
+            max(min(static_cast<int64_t>(row) + p.causal_shift - j * kKeyBlock, static_cast<int64_t>(kKeyBlock)),
+                static_cast<int64_t>(-1)));
         if (lim < kKeyBlock - 1) {
 #pragma unroll
           for (int i = 0; i < kKeyBlock / 2; ++i) {
@@ -512,7 +549,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ok = fold_pv<D>(o, pv_full + 8 * (t), pv_free + 8 * (t), nbt - 1, tm_pv, pend_w, lane, budget, status, abort_flag);
     bias_acc = fmaf(kBias, pend_w, bias_acc);
 
-    if (ok && valid_row && flag_get(abort_flag) == 0) {
+    if (ok && valid_row && flag_get(abort_flag) == 0 && (p.state_mode & kStateStore)) {
+      float4* so = reinterpret_cast<float4*>(p.state_o + (bh * p.nq + row) * D);
+#pragma unroll
+      for (int i = 0; i < D / 4; ++i)
+        so[i] = make_float4(o[2 * i].x - bias_acc, o[2 * i].y - bias_acc, o[2 * i + 1].x - bias_acc,
+                            o[2 * i + 1].y - bias_acc);
+      reinterpret_cast<float2*>(p.state_ml)[bh * p.nq + row] = make_float2(m_ref, l_run);
+    } else if (ok && valid_row && flag_get(abort_flag) == 0) {
       const float inv = 1.0f / fmaxf(l_run, 1e-30f);
       const float* vm = p.vmean + bh * D;
       uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq + row) * D);

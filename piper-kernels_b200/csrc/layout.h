@@ -2,17 +2,21 @@
 //
 // One contiguous caller-owned device buffer holds every intermediate of a
 // piper_attention call.  Region offsets are 256-byte aligned.  Sizes for a
-// problem (B,H,Nq,Nk,D) with BH = B*H:
+// problem (B,H,Nq,Nk,D) with BH = B*H, in address order:
 //   q8      int8  [BH, Nq, D]                 Q codes (row-major, per-32-row scale)
+//   qscale  f32   [BH, ceil(Nq/32)]           Q group scales   (reference: query_scale)
+//   -- K/V pack: k8 .. vrcp are one contiguous span (kv_pack, kv_pack_bytes),
+//      the unit a sequence-sharded ring passes from rank to rank --
 //   k8      int8  [BH, Nk, D]                 centered-K codes (per-64-row scale)
 //   v8t     int8  [BH, D, Nk_pad]             V codes transposed: keys contiguous
-//   qscale  f32   [BH, ceil(Nq/32)]           Q group scales   (reference: query_scale)
 //   kscale  f32   [BH, ceil(Nk/64)]           K group scales   (reference: key_scale)
 //   vscale  f32   [BH, Nk_pad]                V row scales     (reference: value_scale)
 //   vlog2   f32   [BH, Nk_pad]                log2(vscale); -inf on padded keys
 //   vrcp    f32   [BH, Nk_pad]                1/vscale; 0 on padded keys
+//   -- end of the K/V pack --
 //   kmean   f32   [BH, D]                     K sequence mean
 //   vmean   f32   [BH, D]                     V sequence mean (zeros when causal)
+//   totals  f64   [2, BH, D]                  K and V column sums of a sequence shard
 //   ksum    f64   [BH, chunks, D]             per-chunk partial sums of K
 //   vsum    f64   [BH, chunks, D]             per-chunk partial sums of V
 //   counter u32   [BH]                        chunk-completion counters
@@ -45,15 +49,18 @@ inline piper_b200_workspace_layout_t make_layout(int64_t bh, int64_t nq, int64_t
     return at;
   };
   L.q8 = take(static_cast<uint64_t>(bh * nq * d));
+  L.qscale = take(static_cast<uint64_t>(bh * L.q_groups) * 4);
   L.k8 = take(static_cast<uint64_t>(bh * nk * d));
   L.v8t = take(static_cast<uint64_t>(bh * d * L.nk_pad));
-  L.qscale = take(static_cast<uint64_t>(bh * L.q_groups) * 4);
   L.kscale = take(static_cast<uint64_t>(bh * L.k_groups) * 4);
   L.vscale = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
   L.vlog2 = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
   L.vrcp = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
+  L.kv_pack = L.k8;
+  L.kv_pack_bytes = off - L.k8;
   L.kmean = take(static_cast<uint64_t>(bh * d) * 4);
   L.vmean = take(static_cast<uint64_t>(bh * d) * 4);
+  L.totals = take(static_cast<uint64_t>(2 * bh * d) * 8);
   L.ksum = take(static_cast<uint64_t>(bh * L.chunks * d) * 8);
   L.vsum = take(static_cast<uint64_t>(bh * L.chunks * d) * 8);
   L.counter = take(static_cast<uint64_t>(bh) * 4);

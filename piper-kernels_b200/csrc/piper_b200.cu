@@ -128,28 +128,173 @@ bool aligned16(const void* p, const int64_t s[3]) {
   return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && s[0] % 8 == 0 && s[1] % 8 == 0 && s[2] % 8 == 0;
 }
 
+// Which prepass kernels a call runs.
+enum PrepassPart { kSums = 1, kFinalize = 2, kQuantize = 4 };
+
 template <typename T, int D, bool V16>
-void launch_prepass_t(const piper::PrepassArgs& a, int64_t bh, cudaStream_t stream) {
-  const dim3 sum_grid(static_cast<unsigned>(a.L.chunks), static_cast<unsigned>(bh));
-  piper::kv_sum_kernel<T, D, V16><<<sum_grid, piper::kPrepassThreads, 0, stream>>>(a);
-  const int64_t tiles = (std::max(a.nq, a.nk) + piper::kKeyBlock - 1) / piper::kKeyBlock;
-  const dim3 q_grid(static_cast<unsigned>(tiles), static_cast<unsigned>(bh));
-  piper::quantize_kernel<T, D, V16><<<q_grid, piper::kPrepassThreads, 0, stream>>>(a);
+void launch_prepass_t(const piper::PrepassArgs& a, int64_t bh, int parts, cudaStream_t stream) {
+  if (parts & kSums) {
+    const dim3 sum_grid(static_cast<unsigned>(a.L.chunks), static_cast<unsigned>(bh));
+    piper::kv_sum_kernel<T, D, V16><<<sum_grid, piper::kPrepassThreads, 0, stream>>>(a);
+  }
+  if (parts & kFinalize) piper::finalize_means_kernel<D><<<static_cast<unsigned>(bh), D, 0, stream>>>(a);
+  if (parts & kQuantize) {
+    const int64_t tiles = (std::max(a.nq, a.nk) + piper::kKeyBlock - 1) / piper::kKeyBlock;
+    const dim3 q_grid(static_cast<unsigned>(tiles), static_cast<unsigned>(bh));
+    piper::quantize_kernel<T, D, V16><<<q_grid, piper::kPrepassThreads, 0, stream>>>(a);
+  }
 }
 
 template <typename T, int D>
-void launch_prepass_d(const piper::PrepassArgs& a, int64_t bh, bool v16, cudaStream_t stream) {
+void launch_prepass_d(const piper::PrepassArgs& a, int64_t bh, bool v16, int parts, cudaStream_t stream) {
   if (v16)
-    launch_prepass_t<T, D, true>(a, bh, stream);
+    launch_prepass_t<T, D, true>(a, bh, parts, stream);
   else
-    launch_prepass_t<T, D, false>(a, bh, stream);
+    launch_prepass_t<T, D, false>(a, bh, parts, stream);
+}
+
+// Shared argument checks and launches of the prepass entry points.
+// `parts` selects the kernels; `sums_only` makes the mean pass write the
+// shard's fp64 totals; `total_keys` is the mean's denominator for kFinalize.
+int run_prepass(const void* query, const int64_t query_strides[3], const void* key, const int64_t key_strides[3],
+                const void* value, const int64_t value_strides[3], int dtype, int64_t batch, int64_t heads,
+                int64_t query_length, int64_t key_length, int64_t head_dim, int is_causal, void* workspace,
+                size_t workspace_bytes, void* stream, int parts, int sums_only, int64_t total_keys) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!key || !value || !workspace || !key_strides || !value_strides)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  if ((parts & kQuantize) && (!query || !query_strides))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
+  if (workspace_bytes < L.total_bytes)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
+                "workspace needs " + std::to_string(L.total_bytes) + " bytes, got " + std::to_string(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  piper::PrepassArgs a{};
+  a.q = query;
+  a.k = key;
+  a.v = value;
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = query_strides ? query_strides[i] : 0;
+    a.ks[i] = key_strides[i];
+    a.vs[i] = value_strides[i];
+  }
+  a.heads = heads;
+  a.nq = query_length;
+  a.nk = key_length;
+  a.causal = is_causal ? 1 : 0;
+  a.sums_only = sums_only;
+  a.total_keys = total_keys;
+  a.ws = static_cast<uint8_t*>(workspace);
+  a.L = L;
+  bool v16 = aligned16(key, key_strides) && aligned16(value, value_strides);
+  if (parts & kQuantize) v16 = v16 && aligned16(query, query_strides);
+  if (parts & kSums) PIPER_CUDA(cudaMemsetAsync(a.ws + L.counter, 0, static_cast<size_t>(bh) * 4, s));
+  if (dtype == PIPER_B200_FLOAT16) {
+    if (head_dim == 64)
+      launch_prepass_d<__half, 64>(a, bh, v16, parts, s);
+    else
+      launch_prepass_d<__half, 128>(a, bh, v16, parts, s);
+  } else {
+    if (head_dim == 64)
+      launch_prepass_d<__nv_bfloat16, 64>(a, bh, v16, parts, s);
+    else
+      launch_prepass_d<__nv_bfloat16, 128>(a, bh, v16, parts, s);
+  }
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
+}
+
+// The attention launch shared by the one-shot and the sharded entry points:
+// Q side (codes, scales, V mean) from `workspace`, K/V side from `kv_pack`
+// (a K/V pack laid out as in the workspace of the same shape).
+int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                  int64_t head_dim, double scale, int is_causal, const void* workspace, size_t workspace_bytes,
+                  const void* kv_pack, int64_t causal_shift, float* state, int state_mode, void* stream,
+                  bool sharded = false) {
+  // Sharded causal attention pairs independent query and key shards: only the
+  // one-shard form needs Nq == Nk.
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, sharded ? 0 : is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!workspace || !kv_pack) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  if (!(state_mode & piper::kStateStore) && !out) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL output");
+  if (state_mode != 0 && !state) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL state");
+  if (!(std::isfinite(scale) && scale > 0.0))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "scale must be finite and positive");
+  if (out && reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "output must be 16-byte aligned");
+  if (state && reinterpret_cast<uintptr_t>(state) % 16 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(kv_pack) % 256 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "K/V pack must be 256-byte aligned");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
+  if (workspace_bytes < L.total_bytes)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "workspace too small for this problem");
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  const uint8_t* kv = static_cast<const uint8_t*>(kv_pack) - L.kv_pack;  // same offsets as the workspace
+  const uint64_t d = static_cast<uint64_t>(head_dim);
+  CUtensorMap tmQ, tmK, tmV;
+  if ((rc = encode_map(&tmQ, ws + L.q8, d, query_length, bh, d, query_length * d, static_cast<uint32_t>(d),
+                       piper::kTileM)) != PIPER_B200_OK)
+    return rc;
+  if ((rc = encode_map(&tmK, kv + L.k8, d, key_length, bh, d, key_length * d, static_cast<uint32_t>(d),
+                       piper::kKeyBlock)) != PIPER_B200_OK)
+    return rc;
+  if ((rc = encode_map(&tmV, kv + L.v8t, L.nk_pad, d, bh, L.nk_pad, L.nk_pad * d, piper::kKeyBlock,
+                       static_cast<uint32_t>(d))) != PIPER_B200_OK)
+    return rc;
+  piper::AttnParams p{};
+  p.qscale = reinterpret_cast<const float*>(ws + L.qscale);
+  p.kscale = reinterpret_cast<const float*>(kv + L.kscale);
+  p.vlog2 = reinterpret_cast<const float*>(kv + L.vlog2);
+  p.vrcp = reinterpret_cast<const float*>(kv + L.vrcp);
+  p.vmean = reinterpret_cast<const float*>(ws + L.vmean);
+  p.out = out;
+  p.heads = heads;
+  p.nq = query_length;
+  p.nk = key_length;
+  p.nk_pad = L.nk_pad;
+  p.q_groups = L.q_groups;
+  p.k_groups = L.k_groups;
+  p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
+  p.causal = is_causal ? 1 : 0;
+  p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
+  p.wait_budget_ns = piper::kWaitBudgetNs;
+  p.causal_shift = causal_shift;
+  p.state_mode = state_mode;
+  p.state_o = state;
+  p.state_ml = state ? state + bh * query_length * head_dim : nullptr;
+  const dim3 grid(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PIPER_B200_FLOAT16) {
+    if (head_dim == 64)
+      piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+    else
+      piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+  } else {
+    if (head_dim == 64)
+      piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+    else
+      piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+  }
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
 }
 
 }  // namespace
 
 extern "C" {
 
-int piper_b200_abi_version(void) { return 100; }
+int piper_b200_abi_version(void) { return 101; }
 
 const char* piper_b200_last_error(void) { return g_last_error.c_str(); }
 
@@ -185,112 +330,59 @@ int piper_b200_prepass(const void* query, const int64_t query_strides[3], const 
                        const int64_t key_strides[3], const void* value, const int64_t value_strides[3], int dtype,
                        int64_t batch, int64_t heads, int64_t query_length, int64_t key_length, int64_t head_dim,
                        int is_causal, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
-  if (rc != PIPER_B200_OK) return rc;
-  if (!query || !key || !value || !workspace || !query_strides || !key_strides || !value_strides)
-    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
-  int device = 0;
-  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
-  const int64_t bh = batch * heads;
-  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
-  if (workspace_bytes < L.total_bytes)
-    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
-                "workspace needs " + std::to_string(L.total_bytes) + " bytes, got " + std::to_string(workspace_bytes));
-  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
-    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  piper::PrepassArgs a{};
-  a.q = query;
-  a.k = key;
-  a.v = value;
-  for (int i = 0; i < 3; ++i) {
-    a.qs[i] = query_strides[i];
-    a.ks[i] = key_strides[i];
-    a.vs[i] = value_strides[i];
-  }
-  a.heads = heads;
-  a.nq = query_length;
-  a.nk = key_length;
-  a.causal = is_causal ? 1 : 0;
-  a.ws = static_cast<uint8_t*>(workspace);
-  a.L = L;
-  const bool v16 = aligned16(query, query_strides) && aligned16(key, key_strides) && aligned16(value, value_strides);
-  PIPER_CUDA(cudaMemsetAsync(a.ws + L.counter, 0, static_cast<size_t>(bh) * 4, s));
-  if (dtype == PIPER_B200_FLOAT16) {
-    if (head_dim == 64)
-      launch_prepass_d<__half, 64>(a, bh, v16, s);
-    else
-      launch_prepass_d<__half, 128>(a, bh, v16, s);
-  } else {
-    if (head_dim == 64)
-      launch_prepass_d<__nv_bfloat16, 64>(a, bh, v16, s);
-    else
-      launch_prepass_d<__nv_bfloat16, 128>(a, bh, v16, s);
-  }
-  PIPER_CUDA(cudaGetLastError());
-  return PIPER_B200_OK;
+  return run_prepass(query, query_strides, key, key_strides, value, value_strides, dtype, batch, heads, query_length,
+                     key_length, head_dim, is_causal, workspace, workspace_bytes, stream, kSums | kQuantize, 0,
+                     key_length);
 }
 
 int piper_b200_attention_prepared(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
                                   int64_t key_length, int64_t head_dim, double scale, int is_causal,
                                   const void* workspace, size_t workspace_bytes, void* stream) {
+  if (!out || !workspace) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
   int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
   if (rc != PIPER_B200_OK) return rc;
-  if (!out || !workspace) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
-  if (!(std::isfinite(scale) && scale > 0.0))
-    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "scale must be finite and positive");
-  if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
-    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "output must be 16-byte aligned");
-  int device = 0;
-  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
-  const int64_t bh = batch * heads;
-  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
-  if (workspace_bytes < L.total_bytes)
-    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "workspace too small for this problem");
-  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
-  const uint64_t d = static_cast<uint64_t>(head_dim);
-  CUtensorMap tmQ, tmK, tmV;
-  if ((rc = encode_map(&tmQ, ws + L.q8, d, query_length, bh, d, query_length * d, static_cast<uint32_t>(d),
-                       piper::kTileM)) != PIPER_B200_OK)
-    return rc;
-  if ((rc = encode_map(&tmK, ws + L.k8, d, key_length, bh, d, key_length * d, static_cast<uint32_t>(d),
-                       piper::kKeyBlock)) != PIPER_B200_OK)
-    return rc;
-  if ((rc = encode_map(&tmV, ws + L.v8t, L.nk_pad, d, bh, L.nk_pad, L.nk_pad * d, piper::kKeyBlock,
-                       static_cast<uint32_t>(d))) != PIPER_B200_OK)
-    return rc;
-  piper::AttnParams p{};
-  p.qscale = reinterpret_cast<const float*>(ws + L.qscale);
-  p.kscale = reinterpret_cast<const float*>(ws + L.kscale);
-  p.vlog2 = reinterpret_cast<const float*>(ws + L.vlog2);
-  p.vrcp = reinterpret_cast<const float*>(ws + L.vrcp);
-  p.vmean = reinterpret_cast<const float*>(ws + L.vmean);
-  p.out = out;
-  p.heads = heads;
-  p.nq = query_length;
-  p.nk = key_length;
-  p.nk_pad = L.nk_pad;
-  p.q_groups = L.q_groups;
-  p.k_groups = L.k_groups;
-  p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
-  p.causal = is_causal ? 1 : 0;
-  p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
-  p.wait_budget_ns = piper::kWaitBudgetNs;
-  const dim3 grid(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == PIPER_B200_FLOAT16) {
-    if (head_dim == 64)
-      piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-    else
-      piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-  } else {
-    if (head_dim == 64)
-      piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-    else
-      piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-  }
-  PIPER_CUDA(cudaGetLastError());
-  return PIPER_B200_OK;
+  const piper_b200_workspace_layout_t L = piper::make_layout(batch * heads, query_length, key_length, head_dim);
+  return run_attention(out, dtype, batch, heads, query_length, key_length, head_dim, scale, is_causal, workspace,
+                       workspace_bytes, static_cast<const uint8_t*>(workspace) + L.kv_pack, 0, nullptr, 0, stream);
+}
+
+int piper_b200_shard_column_sums(const void* key, const int64_t key_strides[3], const void* value,
+                                 const int64_t value_strides[3], int dtype, int64_t batch, int64_t heads,
+                                 int64_t query_length, int64_t key_length, int64_t head_dim, int is_causal,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return run_prepass(nullptr, nullptr, key, key_strides, value, value_strides, dtype, batch, heads, query_length,
+                     key_length, head_dim, is_causal, workspace, workspace_bytes, stream, kSums, 1, key_length);
+}
+
+int piper_b200_shard_prepass(const void* query, const int64_t query_strides[3], const void* key,
+                             const int64_t key_strides[3], const void* value, const int64_t value_strides[3],
+                             int dtype, int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                             int64_t head_dim, int is_causal, int64_t total_keys, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (total_keys < key_length)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "total_keys must be at least this shard's key length");
+  return run_prepass(query, query_strides, key, key_strides, value, value_strides, dtype, batch, heads,
+                     query_length, key_length, head_dim, is_causal, workspace, workspace_bytes, stream,
+                     kFinalize | kQuantize, 0, total_keys);
+}
+
+int piper_b200_attention_shard(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                               int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                               int64_t causal_shift, const void* workspace, size_t workspace_bytes,
+                               const void* kv_pack, float* state, int state_mode, void* stream) {
+  if (state_mode < 0 || state_mode > (PIPER_B200_STATE_LOAD | PIPER_B200_STATE_STORE))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "state_mode must combine PIPER_B200_STATE_LOAD/STORE");
+  if (!is_causal && causal_shift != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "causal_shift applies to causal attention only");
+  if (is_causal && (causal_shift < -(int64_t(1) << 40) || causal_shift > (int64_t(1) << 40)))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "causal_shift out of range");
+  return run_attention(out, dtype, batch, heads, query_length, key_length, head_dim, scale, is_causal, workspace,
+                       workspace_bytes, kv_pack, causal_shift, state, state_mode, stream, true);
+}
+
+size_t piper_b200_state_bytes(int64_t batch, int64_t heads, int64_t query_length, int64_t head_dim) {
+  if (batch <= 0 || heads <= 0 || query_length <= 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(batch * heads * query_length * (head_dim + 2) * 4);
 }
 
 int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], const void* key,

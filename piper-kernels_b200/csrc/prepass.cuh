@@ -16,7 +16,10 @@
 //                      exact fp64 column sums per 512-row chunk; the last
 //                      chunk of each (b,h) to finish turns the partial sums
 //                      into fp32 means (fixed order, so results are
-//                      deterministic).
+//                      deterministic).  For a sequence shard it writes
+//                      the shard's fp64 column totals instead; the caller
+//                      sums them over the ranks and finalize_means_kernel
+//                      divides by the total key count.
 //   quantize_kernel    grid (ceil(max(Nq,Nk)/64), B*H): one 64-row tile of Q,
 //                      K and V per CTA; group amax via warp shuffles + shared
 //                      memory; V codes transposed to [D, keys] through shared
@@ -88,7 +91,9 @@ struct PrepassArgs {
   int64_t qs[3], ks[3], vs[3];  // B, H, N strides in elements
   int64_t heads, nq, nk;
   int causal;
-  uint8_t* ws;  // workspace base
+  int sums_only;       // kv_sum_kernel: write the shard's fp64 totals, not means
+  int64_t total_keys;  // finalize_means_kernel: keys over all shards
+  uint8_t* ws;         // workspace base
   piper_b200_workspace_layout_t L;
 };
 
@@ -159,17 +164,42 @@ __global__ void __launch_bounds__(kPrepassThreads) kv_sum_kernel(PrepassArgs a) 
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  float* kmean = reinterpret_cast<float*>(a.ws + a.L.kmean);
-  float* vmean = reinterpret_cast<float*>(a.ws + a.L.vmean);
   if (tid < D) {
     double s = 0.0, t = 0.0;
     for (int64_t c = 0; c < chunks; ++c) {
       s += __ldcg(&kpart[(bh * chunks + c) * D + tid]);
       if (with_v) t += __ldcg(&vpart[(bh * chunks + c) * D + tid]);
     }
-    kmean[bh * D + tid] = static_cast<float>(s / static_cast<double>(a.nk));
-    vmean[bh * D + tid] = with_v ? static_cast<float>(t / static_cast<double>(a.nk)) : 0.0f;
+    if (a.sums_only) {
+      // A sequence shard: its totals are summed over the ranks by the caller
+      // and turned into means by finalize_means_kernel.
+      double* totals = reinterpret_cast<double*>(a.ws + a.L.totals);
+      const int64_t bh_all = static_cast<int64_t>(gridDim.y);
+      totals[bh * D + tid] = s;
+      totals[(bh_all + bh) * D + tid] = with_v ? t : 0.0;
+    } else {
+      float* kmean = reinterpret_cast<float*>(a.ws + a.L.kmean);
+      float* vmean = reinterpret_cast<float*>(a.ws + a.L.vmean);
+      kmean[bh * D + tid] = static_cast<float>(s / static_cast<double>(a.nk));
+      vmean[bh * D + tid] = with_v ? static_cast<float>(t / static_cast<double>(a.nk)) : 0.0f;
+    }
   }
+}
+
+// Means of a sequence-sharded problem from the K and V column totals summed
+// over every shard: the same fp64 division and single rounding to fp32 as the
+// one-GPU finalize above.  grid (B*H), D threads.
+template <int D>
+__global__ void __launch_bounds__(D) finalize_means_kernel(PrepassArgs a) {
+  const int64_t bh = blockIdx.x;
+  const int64_t bh_all = static_cast<int64_t>(gridDim.x);
+  const int tid = threadIdx.x;
+  const double* totals = reinterpret_cast<const double*>(a.ws + a.L.totals);
+  float* kmean = reinterpret_cast<float*>(a.ws + a.L.kmean);
+  float* vmean = reinterpret_cast<float*>(a.ws + a.L.vmean);
+  const double n = static_cast<double>(a.total_keys);
+  kmean[bh * D + tid] = static_cast<float>(totals[bh * D + tid] / n);
+  vmean[bh * D + tid] = a.causal ? 0.0f : static_cast<float>(totals[(bh_all + bh) * D + tid] / n);
 }
 
 // ---------------------------------------------------------------------------

@@ -28,6 +28,8 @@ ERR_WORKSPACE_TOO_SMALL = 5
 FLOAT16 = 0
 BFLOAT16 = 1
 NO_ALLOC_WORKSPACE_BYTES = 16 * 1024 * 1024  # PIPER_B200_NO_ALLOC_WORKSPACE_BYTES
+STATE_LOAD = 1  # PIPER_B200_STATE_LOAD
+STATE_STORE = 2  # PIPER_B200_STATE_STORE
 
 # Every symbol include/piper_b200.h declares (tests check the library exports them).
 EXPORTED_SYMBOLS = (
@@ -40,6 +42,10 @@ EXPORTED_SYMBOLS = (
     "piper_b200_attention_prepared",
     "piper_b200_attention_fwd",
     "piper_b200_attention_fwd_no_alloc",
+    "piper_b200_shard_column_sums",
+    "piper_b200_shard_prepass",
+    "piper_b200_attention_shard",
+    "piper_b200_state_bytes",
     "piper_b200_device_status",
     "piper_b200_selftest_wait_timeout",
     "piper_b200_selftest_gemm_i8",
@@ -59,7 +65,9 @@ class WorkspaceLayout(ctypes.Structure):
             "q8", "k8", "v8t", "qscale", "kscale", "vscale", "vlog2", "vrcp",
             "kmean", "vmean", "ksum", "vsum", "counter", "total_bytes",
         )
-    ] + [(name, ctypes.c_int64) for name in ("q_groups", "k_groups", "nk_pad", "chunks")]
+    ] + [(name, ctypes.c_int64) for name in ("q_groups", "k_groups", "nk_pad", "chunks")] + [
+        (name, ctypes.c_uint64) for name in ("kv_pack", "kv_pack_bytes", "totals")
+    ]
 
 
 _lock = threading.Lock()
@@ -95,6 +103,20 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_double, ctypes.c_int, _VP,
     ]
     lib.piper_b200_attention_fwd_no_alloc.restype = ctypes.c_int
+    lib.piper_b200_shard_column_sums.argtypes = [_VP, _STRIDES, _VP, _STRIDES, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_shard_column_sums.restype = ctypes.c_int
+    lib.piper_b200_shard_prepass.argtypes = tensor3 + [ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_int, _I64, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_shard_prepass.restype = ctypes.c_int
+    lib.piper_b200_attention_shard.argtypes = [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _I64, _VP, ctypes.c_size_t, _VP, _VP, ctypes.c_int, _VP,
+    ]
+    lib.piper_b200_attention_shard.restype = ctypes.c_int
+    lib.piper_b200_state_bytes.argtypes = [_I64] * 4
+    lib.piper_b200_state_bytes.restype = ctypes.c_size_t
     lib.piper_b200_device_status.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
     lib.piper_b200_device_status.restype = ctypes.c_int
     lib.piper_b200_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int), _VP]

@@ -102,6 +102,18 @@ class PreparedPiperAttention:
         b, h, _nq, _nk, d = self.shape
         return self._view(self.layout.vmean, b * h * d, torch.float32, (b, h, d))
 
+    @property
+    def kv_pack(self) -> torch.Tensor:
+        """The K/V operands of this workspace as one contiguous byte span."""
+        off = int(self.layout.kv_pack)
+        return self.workspace[off : off + int(self.layout.kv_pack_bytes)]
+
+    @property
+    def column_totals(self) -> torch.Tensor:
+        """fp64 ``[2,B,H,D]`` K and V column sums written by :func:`shard_column_sums`."""
+        b, h, _nq, _nk, d = self.shape
+        return self._view(self.layout.totals, 2 * b * h * d, torch.float64, (2, b, h, d))
+
 
 def workspace_bytes(batch: int, heads: int, nq: int, nk: int, d: int) -> int:
     return int(_native.workspace_layout(batch, heads, nq, nk, d).total_bytes)
@@ -184,6 +196,100 @@ def run_piper_attention(
             "piper_b200_attention_fwd",
         )
     return out
+
+
+def shard_column_sums(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    is_causal: bool,
+    *,
+    workspace: torch.Tensor | None = None,
+) -> PreparedPiperAttention:
+    """First step of a sequence shard's prepass: its fp64 K/V column totals.
+
+    The totals (``.column_totals``) are to be summed over all shards before
+    :func:`shard_prepass`.  ``query`` only fixes the workspace shape.
+    """
+    lib = _native.library()
+    b, h, nq, d = query.shape
+    nk = key.shape[2]
+    layout = _native.workspace_layout(b, h, nq, nk, d)
+    if workspace is None:
+        workspace = torch.empty(int(layout.total_bytes), dtype=torch.uint8, device=query.device)
+    with torch.cuda.device(query.device):
+        _native.check(
+            lib.piper_b200_shard_column_sums(
+                _ptr(key), _native.strides3(key), _ptr(value), _native.strides3(value),
+                _DTYPE_CODES[query.dtype], b, h, nq, nk, d, 1 if is_causal else 0,
+                _ptr(workspace), workspace.numel(), _stream(query.device),
+            ),
+            "piper_b200_shard_column_sums",
+        )
+    return PreparedPiperAttention(workspace, layout, (b, h, nq, nk, d), query.dtype, is_causal)
+
+
+def shard_prepass(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    prepared: PreparedPiperAttention,
+    total_keys: int,
+) -> PreparedPiperAttention:
+    """Means from the (already summed) column totals, then this shard's codes."""
+    lib = _native.library()
+    b, h, nq, nk, d = prepared.shape
+    with torch.cuda.device(query.device):
+        _native.check(
+            lib.piper_b200_shard_prepass(
+                _ptr(query), _native.strides3(query), _ptr(key), _native.strides3(key),
+                _ptr(value), _native.strides3(value), _DTYPE_CODES[query.dtype],
+                b, h, nq, nk, d, 1 if prepared.is_causal else 0, int(total_keys),
+                _ptr(prepared.workspace), prepared.workspace.numel(), _stream(query.device),
+            ),
+            "piper_b200_shard_prepass",
+        )
+    return prepared
+
+
+def state_bytes(batch: int, heads: int, nq: int, d: int) -> int:
+    return int(_native.library().piper_b200_state_bytes(batch, heads, nq, d))
+
+
+def attention_shard(
+    prepared: PreparedPiperAttention,
+    kv_pack: torch.Tensor,
+    scale: float,
+    *,
+    key_length: int | None = None,
+    state: torch.Tensor | None = None,
+    state_mode: int = 0,
+    causal_shift: int = 0,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor | None:
+    """Attention of this shard's queries over one shard of keys (a K/V pack).
+
+    ``state`` (fp32, :func:`state_bytes` bytes) carries the per-row softmax
+    state between key shards; see ``piper_b200_attention_shard``.  Returns the
+    output unless ``state_mode`` stores the state instead.
+    """
+    lib = _native.library()
+    b, h, nq, nk, d = prepared.shape
+    nk = nk if key_length is None else int(key_length)
+    device = prepared.workspace.device
+    if out is None and not state_mode & _native.STATE_STORE:
+        out = torch.empty((b, h, nq, d), dtype=prepared.dtype, device=device)
+    with torch.cuda.device(device):
+        _native.check(
+            lib.piper_b200_attention_shard(
+                None if out is None else _ptr(out), _DTYPE_CODES[prepared.dtype], b, h, nq, nk, d, float(scale),
+                1 if prepared.is_causal else 0, int(causal_shift), _ptr(prepared.workspace),
+                prepared.workspace.numel(), _ptr(kv_pack), None if state is None else _ptr(state),
+                int(state_mode), _stream(device),
+            ),
+            "piper_b200_attention_shard",
+        )
+    return None if state_mode & _native.STATE_STORE else out
 
 
 @torch.library.custom_op("piper_kernels::piper_attention", mutates_args=())

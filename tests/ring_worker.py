@@ -1,0 +1,55 @@
+"""One rank of the NCCL ring check (launched by test_gpu_ring.py under torchrun).
+
+Every rank builds the same full sequence from one seed, runs
+``ring_piper_attention`` on its rows over NCCL, and compares them with the
+one-GPU operator on the whole sequence, computed on its own GPU.  Prints
+RING_OK on success; any mismatch raises (non-zero exit).
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parents[1]
+for _p in (REPO / "piper-kernels_b200", REPO):
+    sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from piper_kernels import piper_attention  # noqa: E402
+from piper_kernels.attention.piper_attention import ring_piper_attention  # noqa: E402
+
+
+def main() -> None:
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    try:
+        for is_causal, dtype, n_shard in ((False, torch.bfloat16, 2048), (True, torch.float16, 1024)):
+            g = torch.Generator(device=dev).manual_seed(123)
+            shape = (1, 4, n_shard * world, 128)
+            q = torch.randn(shape, generator=g, device=dev).to(dtype)
+            k = (torch.randn(shape, generator=g, device=dev) + 1.0).to(dtype)
+            v = (torch.randn(shape, generator=g, device=dev) + 0.5).to(dtype)
+            rows = slice(rank * n_shard, (rank + 1) * n_shard)
+            with torch.no_grad():
+                mine = ring_piper_attention(q[:, :, rows], k[:, :, rows], v[:, :, rows], is_causal=is_causal)
+                whole = piper_attention(q, k, v, is_causal=is_causal)[:, :, rows]
+            torch.cuda.synchronize()
+            err = (mine.float() - whole.float()).abs()
+            if not (err.max().item() < 0.02 and err.mean().item() < 2e-4):
+                raise AssertionError(f"rank {rank} causal={is_causal}: max {err.max().item()} mean {err.mean().item()}")
+        dist.barrier(device_ids=[local])
+        print("RING_OK", rank, flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,173 @@
+"""Host logic of the sequence-sharded ring on CPU: ``gloo`` ranks, oracle compute.
+
+The ring driver (``ring_piper_attention``) takes its compute steps from a
+``ShardOps`` object; here that object is the CPU oracle (a test double that
+stands where the sm_100a library does on a GPU), so these tests check what the
+host side decides: the all-reduced column totals and the means made from
+them, which pack each rank holds at each step, the double-buffered exchange,
+the state modes and the causal shifts.  Each rank's rows must match the
+one-shot oracle on the whole sequence (codes bit for bit, outputs to fp32
+rounding), for 2, 3 and 4 ranks, causal and not.
+"""
+
+from __future__ import annotations
+
+import socket
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle
+from piper_kernels.attention.piper_attention.ring import ring_piper_attention
+
+
+class OracleShardOps:
+    """``ShardOps`` over the CPU oracle; packs are serialised to uint8 tensors."""
+
+    instances: list["OracleShardOps"] = []
+
+    def __init__(self, query, key, value, is_causal, scale):
+        self.q, self.k, self.v = query, key, value
+        self.is_causal = is_causal
+        self.scale = scale
+        self.b, self.h, self.n, self.d = query.shape
+        self.prepared = None
+        OracleShardOps.instances.append(self)
+
+    def column_totals(self):
+        # The driver all-reduces this tensor in place; quantize reads it back.
+        kt = self.k.double().sum(dim=2)
+        vt = torch.zeros_like(kt) if self.is_causal else self.v.double().sum(dim=2)
+        self.totals = torch.stack([kt, vt])
+        return self.totals
+
+    def quantize(self, total_keys):
+        km = (self.totals[0].numpy() / float(total_keys)).astype(np.float32)
+        vm = None if self.is_causal else (self.totals[1].numpy() / float(total_keys)).astype(np.float32)
+        self.prepared = oracle.prepare(self.q, self.k, self.v, self.is_causal, key_mean=km, value_mean=vm)
+
+    def _pieces(self):
+        p = self.prepared
+        return [p.key_int8, p.key_scale, p.value_int8, p.value_scale]
+
+    def local_pack(self):
+        raw = b"".join(np.ascontiguousarray(a).tobytes() for a in self._pieces())
+        return torch.frombuffer(bytearray(raw), dtype=torch.uint8)
+
+    def empty_pack(self):
+        return torch.empty_like(self.local_pack())
+
+    def _unpack(self, pack):
+        data = pack.numpy().tobytes()
+        out, at = [], 0
+        for ref in self._pieces():
+            nbytes = ref.nbytes
+            out.append(np.frombuffer(data[at : at + nbytes], dtype=ref.dtype).reshape(ref.shape))
+            at += nbytes
+        assert at == len(data)
+        k8, ks, v8, vs = out
+        return SimpleNamespace(key_int8=k8, key_scale=ks, value_int8=v8, value_scale=vs)
+
+    def new_state(self):
+        return torch.zeros(self.b * self.h * self.n * (self.d + 2), dtype=torch.float32)
+
+    def attend(self, pack, state, state_mode, causal_shift, out):
+        pair = None
+        if state is not None:
+            cut = self.b * self.h * self.n * self.d
+            arr = state.numpy()
+            pair = (arr[:cut].reshape(self.b, self.h, self.n, self.d), arr[cut:].reshape(self.b, self.h, self.n, 2))
+        result = oracle.attention_shard(self.prepared, self._unpack(pack), self.scale, self.is_causal,
+                                        causal_shift=causal_shift, state=pair, state_mode=state_mode)
+        if result is not None:
+            out.copy_(torch.from_numpy(result).to(out.dtype))
+
+
+def _inputs(n_total: int, d: int, dtype):
+    g = torch.Generator().manual_seed(n_total + d)
+    q = torch.randn((1, 2, n_total, d), generator=g).to(dtype)
+    k = (torch.randn((1, 2, n_total, d), generator=g) + torch.randn((1, 2, 1, d), generator=g) * 2).to(dtype)
+    v = (torch.randn((1, 2, n_total, d), generator=g) + torch.randn((1, 2, 1, d), generator=g)).to(dtype)
+    return q, k, v
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, n_shard: int, d: int, is_causal: bool) -> None:
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        oracle.set_threads(1)
+        q, k, v = _inputs(n_shard * world, d, torch.float16)
+        rows = slice(rank * n_shard, (rank + 1) * n_shard)
+        with torch.no_grad():
+            out = ring_piper_attention(q[:, :, rows], k[:, :, rows], v[:, :, rows], is_causal=is_causal,
+                                       ops_factory=OracleShardOps)
+        full, prepared = oracle.piper_attention(q, k, v, None, is_causal)
+        mine = OracleShardOps.instances[-1].prepared
+        assert np.array_equal(mine.key_mean, prepared.key_mean)
+        assert np.array_equal(mine.query_int8, prepared.query_int8[:, :, rows])
+        assert np.array_equal(mine.key_int8, prepared.key_int8[:, :, rows])
+        assert np.array_equal(mine.key_scale, prepared.key_scale[:, :, rank * n_shard // 64 : (rank + 1) * n_shard // 64])
+        assert np.array_equal(mine.value_int8, prepared.value_int8[:, :, rows])
+        assert np.array_equal(mine.value_scale, prepared.value_scale[:, :, rows])
+        expected = torch.from_numpy(full[:, :, rows]).to(out.dtype).float()
+        err = (out.float() - expected).abs()
+        # The re-associated recurrence differs from the one-shot one by fp32
+        # rounding only: after the cast to fp16 at most one ulp, rarely.
+        assert err.max().item() <= 2e-3 * max(1.0, expected.abs().max().item()), err.max().item()
+        assert (err > 0).float().mean().item() < 1e-3
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_ring_matches_one_shot_oracle(world: int, is_causal: bool) -> None:
+    mp.spawn(_worker, args=(world, _free_port(), 128, 64, is_causal), nprocs=world, join=True)
+
+
+def _mismatch_worker(rank: int, world: int, port: int, case: str) -> None:
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        n = 128
+        if case == "shape" and rank == 1:
+            n = 192
+        if case == "alignment":
+            n = 100
+        q, k, v = _inputs(n, 64, torch.float16)
+        if case == "dtype" and rank == 0:
+            v = v.to(torch.bfloat16)
+        expected = {
+            "shape": "same \\[B, H, N, D\\] shard shape",
+            "alignment": "multiple of 64 rows",
+            "dtype": "share a dtype" if rank == 0 else "another rank rejected",
+        }[case]
+        with torch.no_grad(), pytest.raises(ValueError, match=expected):
+            ring_piper_attention(q, k, v, ops_factory=OracleShardOps)
+        # Every rank left together: the group still works.
+        t = torch.ones(1)
+        dist.all_reduce(t)
+        assert t.item() == world
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["shape", "alignment", "dtype"])
+def test_ring_rejects_inputs_on_every_rank(case: str) -> None:
+    mp.spawn(_mismatch_worker, args=(2, _free_port(), case), nprocs=2, join=True)
+
+
+def test_single_process_ring_is_the_one_shot_operator() -> None:
+    q, k, v = _inputs(200, 64, torch.bfloat16)
+    with torch.no_grad():
+        out = ring_piper_attention(q, k, v, is_causal=True, ops_factory=OracleShardOps)
+    expected = oracle.piper_attention_torch(q, k, v, None, True)
+    assert torch.equal(out, expected)
