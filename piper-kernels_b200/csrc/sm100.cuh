@@ -96,13 +96,17 @@ __device__ __forceinline__ void flag_set(uint32_t addr, uint32_t v) {
 // (after recording `status_bit` in *status and raising the abort flag) when
 // `budget_ns` of wall-clock time passes first, or as soon as another warp
 // has raised the abort flag.
+//
+// The probe is the non-suspending test_wait: a suspended warp is woken
+// noticeably later than a spinning one sees the phase flip, and every waiter
+// here sits on the critical path of the pipeline.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t budget_ns, uint32_t* status,
                                           uint32_t status_bit, uint32_t abort_addr) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test(bar, parity)) return true;
     if ((++spins & 3u) == 0) {
       if (abort_addr != 0 && flag_get(abort_addr) != 0) return false;
       if (global_timer_ns() - start > budget_ns) {
