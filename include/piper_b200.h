@@ -156,6 +156,27 @@ int piper_b200_attention_shard(void* out, int dtype, int64_t batch, int64_t head
 size_t piper_b200_state_bytes(int64_t batch, int64_t heads, int64_t query_length,
                               int64_t head_dim);
 
+/* ---- Host-to-host forward pass -----------------------------------------
+ * piper_b200_attention_fwd for inputs and output in HOST memory (contiguous
+ * [B, H, N, D]; page-locked memory is needed for the copies to overlap).  No
+ * counterpart in the reference, where the caller moves tensors to the GPU
+ * first.  The heads are processed in chunks through a ring of device slots:
+ * host-to-device copies, the kernels and device-to-host copies of different
+ * chunks overlap, so the call costs about the slowest of the three rather
+ * than their sum.  `scratch` is device memory of piper_b200_host_scratch_bytes
+ * bytes (256-byte aligned).  Kernels run on `stream` and on an internal
+ * stream, the copies on two more internal streams, all ordered after the work
+ * already on `stream`; `stream` is made to wait for the last output copy, so
+ * synchronising `stream` (or an event recorded on it) means `out` is
+ * complete. */
+int piper_b200_host_scratch_bytes(int64_t batch, int64_t heads, int64_t query_length,
+                                  int64_t key_length, int64_t head_dim, size_t* bytes);
+
+int piper_b200_attention_fwd_host(const void* query, const void* key, const void* value, void* out,
+                                  int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                                  int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                                  void* scratch, size_t scratch_bytes, void* stream);
+
 /* Scratch capacity of piper_b200_attention_fwd_no_alloc: 16 MiB per GPU. */
 #define PIPER_B200_NO_ALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)
 

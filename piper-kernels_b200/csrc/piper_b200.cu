@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -521,4 +522,201 @@ extern "C" int piper_b200_attention_fwd_no_alloc(const void* query, const int64_
   return piper_b200_attention_fwd(query, query_strides, key, key_strides, value, value_strides, out, dtype, batch,
                                   heads, query_length, key_length, head_dim, scale, is_causal, workspace,
                                   PIPER_B200_NO_ALLOC_WORKSPACE_BYTES, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Host-to-host forward pass (piper_b200_attention_fwd_host).
+//
+// The heads are split into chunks; each chunk goes through a ring of
+// kHostSlots device slots: H2D copy of its Q/K/V on a copy stream, prepass +
+// attention on one of two compute streams (the caller's and an internal one,
+// alternating, so one chunk's kernels fill the SMs the other's wave tail
+// leaves idle), D2H copy of its output on a second copy stream.  Copies in
+// both directions overlap the kernels of other chunks, so the call takes
+// about max(H2D, compute, D2H) instead of their sum.
+namespace {
+
+constexpr int kHostSlots = 4;
+
+constexpr int kMaxHostChunks = 4096;
+
+struct HostPlan {
+  int64_t heads_per_slot = 0, chunks = 0;
+  int64_t chunk_h0[kMaxHostChunks], chunk_heads[kMaxHostChunks];
+  uint64_t q_bytes = 0, kv_bytes = 0, out_bytes = 0, ws_bytes = 0;  // per slot (heads_per_slot heads)
+  uint64_t slot_bytes = 0, total_bytes = 0;
+  uint64_t off_q = 0, off_k = 0, off_v = 0, off_out = 0, off_ws = 0;
+};
+
+// The heads are cut into chunks: a first chunk of at most one wave of CTAs
+// (the kernels start as soon as it has landed), then chunks of `hc` heads,
+// and the remainder in one-wave chunks (everything after the final
+// host-to-device copy -- the last chunk's kernels and its copy back -- stays
+// short).  `hc` holds about kHostChunkBytes of inputs, about a millisecond of
+// PCIe traffic (measured best on B200 for B1 H40 N16384 and B4 H32 N8192),
+// at most 16 heads and at most a third of them so that copies and kernels
+// overlap.
+constexpr double kHostChunkBytes = 52e6;
+
+void make_host_plan(int64_t bh, int64_t nq, int64_t nk, int64_t d, int sms, HostPlan* P) {
+  const int64_t q_tiles = (nq + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles);
+  const double head_bytes = static_cast<double>((nq + 2 * nk) * d * 2);
+  const int64_t max_hc = std::max<int64_t>(1, std::min<int64_t>(16, bh / 3));
+  int64_t hc = std::max<int64_t>(1, std::min<int64_t>(max_hc, std::llround(kHostChunkBytes / head_bytes)));
+  hc = std::max<int64_t>(hc, (bh + kMaxHostChunks - 3) / (kMaxHostChunks - 2));
+  const int64_t per_wave = std::max<int64_t>(1, std::min<int64_t>(hc, sms / std::max<int64_t>(q_tiles, 1)));
+  int64_t n = 0, h = 0;
+  auto add = [&](int64_t heads) {
+    P->chunk_h0[n] = h;
+    P->chunk_heads[n++] = heads;
+    h += heads;
+  };
+  add(std::min<int64_t>(per_wave, bh));
+  while (bh - h > hc) add(hc);
+  while (h < bh) add(std::min<int64_t>(per_wave, bh - h));
+  P->chunks = n;
+  P->heads_per_slot = hc;
+  P->q_bytes = static_cast<uint64_t>(hc * nq * d) * 2;
+  P->kv_bytes = static_cast<uint64_t>(hc * nk * d) * 2;
+  P->out_bytes = P->q_bytes;
+  P->ws_bytes = piper::make_layout(hc, nq, nk, d).total_bytes;
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) {
+    const uint64_t at = off;
+    off = piper::align_up(off + bytes, 256);
+    return at;
+  };
+  P->off_q = take(P->q_bytes);
+  P->off_k = take(P->kv_bytes);
+  P->off_v = take(P->kv_bytes);
+  P->off_out = take(P->out_bytes);
+  P->off_ws = take(P->ws_bytes);
+  P->slot_bytes = off;
+  P->total_bytes = P->slot_bytes * kHostSlots;
+}
+
+struct HostStreams {
+  bool ready = false;
+  cudaStream_t h2d = nullptr, d2h = nullptr, compute = nullptr;
+  cudaEvent_t start = nullptr;
+  cudaEvent_t loaded[kHostSlots] = {}, computed[kHostSlots] = {}, drained[kHostSlots] = {};
+  std::mutex enqueue;  // one call at a time enqueues on the shared copy streams
+};
+HostStreams g_host[kMaxDevices];
+
+int host_streams(int device, HostStreams** out) {
+  std::lock_guard<std::mutex> lock(g_init_mutex);
+  HostStreams& h = g_host[device];
+  if (!h.ready) {
+    PIPER_CUDA(cudaStreamCreateWithFlags(&h.h2d, cudaStreamNonBlocking));
+    PIPER_CUDA(cudaStreamCreateWithFlags(&h.d2h, cudaStreamNonBlocking));
+    PIPER_CUDA(cudaStreamCreateWithFlags(&h.compute, cudaStreamNonBlocking));
+    PIPER_CUDA(cudaEventCreateWithFlags(&h.start, cudaEventDisableTiming));
+    for (int i = 0; i < kHostSlots; ++i) {
+      PIPER_CUDA(cudaEventCreateWithFlags(&h.loaded[i], cudaEventDisableTiming));
+      PIPER_CUDA(cudaEventCreateWithFlags(&h.computed[i], cudaEventDisableTiming));
+      PIPER_CUDA(cudaEventCreateWithFlags(&h.drained[i], cudaEventDisableTiming));
+    }
+    h.ready = true;
+  }
+  *out = &h;
+  return PIPER_B200_OK;
+}
+
+int sm_count(int device, int* sms) {
+  PIPER_CUDA(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, device));
+  return PIPER_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int piper_b200_host_scratch_bytes(int64_t batch, int64_t heads, int64_t query_length,
+                                             int64_t key_length, int64_t head_dim, size_t* bytes) {
+  if (bytes == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (batch <= 0 || heads <= 0 || query_length <= 0 || key_length <= 0 || head_dim <= 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  // The chunking depends on the SM count of the current device (148 on a
+  // B200, also assumed when no device is visible).
+  int device = 0, sms = 148;
+  if (cudaGetDevice(&device) != cudaSuccess || sm_count(device, &sms) != PIPER_B200_OK) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  HostPlan* plan = new HostPlan;
+  make_host_plan(batch * heads, query_length, key_length, head_dim, sms, plan);
+  *bytes = static_cast<size_t>(plan->total_bytes);
+  delete plan;
+  return PIPER_B200_OK;
+}
+
+extern "C" int piper_b200_attention_fwd_host(const void* query, const void* key, const void* value, void* out,
+                                             int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                                             int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                                             void* scratch, size_t scratch_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!query || !key || !value || !out || !scratch) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  if (!(std::isfinite(scale) && scale > 0.0))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "scale must be finite and positive");
+  if (reinterpret_cast<uintptr_t>(scratch) % 256 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "scratch must be 256-byte aligned");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  int sms = 148;
+  if ((rc = sm_count(device, &sms)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  static thread_local HostPlan plan_storage;  // ~64 KB: kept off the stack
+  HostPlan& P = plan_storage;
+  make_host_plan(bh, query_length, key_length, head_dim, sms, &P);
+  if (scratch_bytes < P.total_bytes)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "scratch needs " + std::to_string(P.total_bytes) + " bytes, got " +
+                                                         std::to_string(scratch_bytes));
+  HostStreams* hs = nullptr;
+  if ((rc = host_streams(device, &hs)) != PIPER_B200_OK) return rc;
+  std::lock_guard<std::mutex> lock(hs->enqueue);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  const uint8_t* hq = static_cast<const uint8_t*>(query);
+  const uint8_t* hk = static_cast<const uint8_t*>(key);
+  const uint8_t* hv = static_cast<const uint8_t*>(value);
+  uint8_t* ho = static_cast<uint8_t*>(out);
+  const uint64_t q_head = static_cast<uint64_t>(query_length * head_dim) * 2;
+  const uint64_t kv_head = static_cast<uint64_t>(key_length * head_dim) * 2;
+  // Nothing of this call may start before the caller's earlier work.
+  PIPER_CUDA(cudaEventRecord(hs->start, s));
+  PIPER_CUDA(cudaStreamWaitEvent(hs->h2d, hs->start, 0));
+  PIPER_CUDA(cudaStreamWaitEvent(hs->d2h, hs->start, 0));
+  PIPER_CUDA(cudaStreamWaitEvent(hs->compute, hs->start, 0));
+  for (int64_t c = 0; c < P.chunks; ++c) {
+    const int slot = static_cast<int>(c % kHostSlots);
+    const int64_t h0 = P.chunk_h0[c];
+    const int64_t hc = P.chunk_heads[c];
+    uint8_t* sb = base + slot * P.slot_bytes;
+    // H2D into the slot once its previous chunk's output has been copied out.
+    if (c >= kHostSlots) PIPER_CUDA(cudaStreamWaitEvent(hs->h2d, hs->drained[slot], 0));
+    PIPER_CUDA(cudaMemcpyAsync(sb + P.off_q, hq + h0 * q_head, hc * q_head, cudaMemcpyHostToDevice, hs->h2d));
+    PIPER_CUDA(cudaMemcpyAsync(sb + P.off_k, hk + h0 * kv_head, hc * kv_head, cudaMemcpyHostToDevice, hs->h2d));
+    PIPER_CUDA(cudaMemcpyAsync(sb + P.off_v, hv + h0 * kv_head, hc * kv_head, cudaMemcpyHostToDevice, hs->h2d));
+    PIPER_CUDA(cudaEventRecord(hs->loaded[slot], hs->h2d));
+    // Kernels on the caller's stream or the internal compute stream (the
+    // chunk is a [1, hc, N, D] problem).
+    cudaStream_t cs = (c & 1) ? hs->compute : s;
+    PIPER_CUDA(cudaStreamWaitEvent(cs, hs->loaded[slot], 0));
+    const int64_t qs[3] = {hc * query_length * head_dim, query_length * head_dim, head_dim};
+    const int64_t ks[3] = {hc * key_length * head_dim, key_length * head_dim, head_dim};
+    const uint64_t ws_bytes = piper::make_layout(hc, query_length, key_length, head_dim).total_bytes;
+    rc = piper_b200_attention_fwd(sb + P.off_q, qs, sb + P.off_k, ks, sb + P.off_v, ks, sb + P.off_out, dtype, 1, hc,
+                                  query_length, key_length, head_dim, scale, is_causal, sb + P.off_ws, ws_bytes, cs);
+    if (rc != PIPER_B200_OK) return rc;
+    PIPER_CUDA(cudaEventRecord(hs->computed[slot], cs));
+    // D2H of the chunk's output.
+    PIPER_CUDA(cudaStreamWaitEvent(hs->d2h, hs->computed[slot], 0));
+    PIPER_CUDA(cudaMemcpyAsync(ho + h0 * q_head, sb + P.off_out, hc * q_head, cudaMemcpyDeviceToHost, hs->d2h));
+    PIPER_CUDA(cudaEventRecord(hs->drained[slot], hs->d2h));
+  }
+  // The caller's stream completes when the last output bytes have landed
+  // (which follows every chunk's kernels, on either compute stream).
+  const int last = static_cast<int>((P.chunks - 1) % kHostSlots);
+  PIPER_CUDA(cudaStreamWaitEvent(s, hs->drained[last], 0));
+  return PIPER_B200_OK;
 }

@@ -46,6 +46,8 @@ EXPORTED_SYMBOLS = (
     "piper_b200_shard_prepass",
     "piper_b200_attention_shard",
     "piper_b200_state_bytes",
+    "piper_b200_host_scratch_bytes",
+    "piper_b200_attention_fwd_host",
     "piper_b200_device_status",
     "piper_b200_selftest_wait_timeout",
     "piper_b200_selftest_gemm_i8",
@@ -117,6 +119,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.piper_b200_attention_shard.restype = ctypes.c_int
     lib.piper_b200_state_bytes.argtypes = [_I64] * 4
     lib.piper_b200_state_bytes.restype = ctypes.c_size_t
+    lib.piper_b200_host_scratch_bytes.argtypes = [_I64] * 5 + [ctypes.POINTER(ctypes.c_size_t)]
+    lib.piper_b200_host_scratch_bytes.restype = ctypes.c_int
+    lib.piper_b200_attention_fwd_host.argtypes = [_VP] * 4 + [ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_attention_fwd_host.restype = ctypes.c_int
     lib.piper_b200_device_status.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
     lib.piper_b200_device_status.restype = ctypes.c_int
     lib.piper_b200_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int), _VP]

@@ -16,6 +16,7 @@ Replaces the reference's Triton backend
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -195,6 +196,65 @@ def run_piper_attention(
             ),
             "piper_b200_attention_fwd",
         )
+    return out
+
+
+def host_scratch_bytes(batch: int, heads: int, nq: int, nk: int, d: int) -> int:
+    size = ctypes.c_size_t(0)
+    _native.check(
+        _native.library().piper_b200_host_scratch_bytes(batch, heads, nq, nk, d, ctypes.byref(size)),
+        "piper_b200_host_scratch_bytes",
+    )
+    return int(size.value)
+
+
+def run_piper_attention_host(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    *,
+    scale: float | None = None,
+    is_causal: bool = False,
+    out: torch.Tensor | None = None,
+    device: torch.device | int | None = None,
+    synchronize: bool = True,
+) -> torch.Tensor:
+    """The forward pass from host tensors to a host tensor (piper_b200_attention_fwd_host).
+
+    ``query``/``key``/``value`` are contiguous CPU tensors (pinned memory lets
+    the copies overlap the kernels); the result is written to ``out`` (a
+    contiguous CPU tensor, pinned by default).  Heads stream through the GPU
+    in chunks, so host-to-device copies, kernels and device-to-host copies
+    overlap.  With ``synchronize=False`` the result is complete once the
+    device's current stream has finished.
+    """
+    from .._validation import validate_attention_inputs
+
+    scale = validate_attention_inputs("piper_attention", query, key, value, scale, is_causal)
+    for name, t in (("query", query), ("key", key), ("value", value)):
+        if t.device.type != "cpu" or not t.is_contiguous():
+            raise ValueError(f"run_piper_attention_host {name} must be a contiguous CPU tensor")
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device("cuda", device).index)
+    b, h, nq, d = query.shape
+    nk = key.shape[2]
+    if out is None:
+        out = torch.empty(query.shape, dtype=query.dtype, pin_memory=True)
+    elif out.device.type != "cpu" or not out.is_contiguous() or out.shape != query.shape or out.dtype != query.dtype:
+        raise ValueError("out must be a contiguous CPU tensor shaped and typed like query")
+    with torch.cuda.device(dev):
+        scratch = torch.empty(host_scratch_bytes(b, h, nq, nk, d), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        _native.check(
+            _native.library().piper_b200_attention_fwd_host(
+                _ptr(query), _ptr(key), _ptr(value), _ptr(out), _DTYPE_CODES[query.dtype], b, h, nq, nk, d,
+                float(scale), 1 if is_causal else 0, _ptr(scratch), scratch.numel(), stream.cuda_stream,
+            ),
+            "piper_b200_attention_fwd_host",
+        )
+        # Freeing `scratch` here is safe: the call made `stream` wait for its
+        # last copy, so whatever reuses the memory on `stream` runs after it.
+        if synchronize:
+            stream.synchronize()
     return out
 
 
