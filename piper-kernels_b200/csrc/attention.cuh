@@ -129,6 +129,33 @@ constexpr uint32_t kBiasBits = 0x4B400000u;
 constexpr float kBias = 12582912.0f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: numerator rescaled only past 2^8 growth
 
+// 2^x for a pair of x <= 0 on the FMA pipe, used for a share of the
+// probabilities so the MUFU pipe (16 ex2 per clock per SM, shared by the two
+// softmax warps of each SMSP) is not the only source (the offload
+// FlashAttention-4 publishes).  Cody-Waite split x = n + f with
+// n = round(x) (the 1.5*2^23 add) and f in [-0.5, 0.5]; 2^f by a degree-5
+// polynomial whose coefficients were fitted here for relative error
+// (iteratively reweighted least squares, 2.3e-7 worst case in fp32 Horner,
+// on a par with ex2.approx); 2^n by adding n to the exponent field (one
+// integer multiply-add).  x is clamped at -126.5: for x = -inf the result is
+// a denormal near 1e-38 instead of 0, which rounds to a zero UINT8 code and
+// is negligible in the denominator.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.5f);
+  x.y = fmaxf(x.y, -126.5f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 u = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(u, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(make_float2(0.001327644451521337f, 0.001327644451521337f), f,
+                        make_float2(0.00967553723603487f, 0.00967553723603487f));
+  p = __ffma2_rn(p, f, make_float2(0.05550713464617729f, 0.05550713464617729f));
+  p = __ffma2_rn(p, f, make_float2(0.24022120237350464f, 0.24022120237350464f));
+  p = __ffma2_rn(p, f, make_float2(0.6931469440460205f, 0.6931469440460205f));
+  p = __ffma2_rn(p, f, make_float2(1.0000001192092896f, 1.0000001192092896f));
+  return make_float2(__uint_as_float(__float_as_uint(t.x) * 0x800000u + __float_as_uint(p.x)),
+                     __uint_as_float(__float_as_uint(t.y) * 0x800000u + __float_as_uint(p.y)));
+}
+
 __device__ __forceinline__ float2 f2(uint32_t a, uint32_t b) {
   return make_float2(__uint_as_float(a), __uint_as_float(b));
 }
@@ -523,7 +550,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           float2 e0 = __fadd2_rn(x[2 * w], mneg);
           float2 e1 = __fadd2_rn(x[2 * w + 1], mneg);
           e0 = make_float2(ex2_approx(e0.x), ex2_approx(e0.y));
-          e1 = make_float2(ex2_approx(e1.x), ex2_approx(e1.y));
+          // One pair in eight on the FMA pipe (measured best: 1/4 and 1/2 are
+          // slower, the kernel is issue-bound more than MUFU-bound).
+          if (q == 0)
+            e1 = exp2_poly2(e1);
+          else
+            e1 = make_float2(ex2_approx(e1.x), ex2_approx(e1.y));
           ps[q] = __ffma2_rn(e0, make_float2(rv.x, rv.y), ps[q]);
           ps[q] = __ffma2_rn(e1, make_float2(rv.z, rv.w), ps[q]);
           const float2 y0 = __ffma2_rn(e0, k255, kb2);
