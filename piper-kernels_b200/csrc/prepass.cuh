@@ -47,37 +47,27 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
 }
 
-// Loads 8 consecutive elements as floats (16 bytes when `kVec16`, else
-// element-wise).
-template <typename T, bool kVec16>
-__device__ __forceinline__ void load8(const T* p, float (&out)[8]) {
-  if constexpr (kVec16) {
-    const int4 raw = __ldg(reinterpret_cast<const int4*>(p));
-    const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) out[i] = to_f32<T>(e[i]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) out[i] = to_f32<T>(p[i]);
-  }
-}
-
 // clamp(round_half_even(x / scale), -127, 127), bit-exact with the IEEE
-// quotient, without a division or a float-to-int conversion per element.
+// quotient, without a division or a float-to-int conversion per element,
+// for a pair of elements at a time (packed f32x2 arithmetic).
 // q = x * (1/scale) (reciprocal correctly rounded) is within
 // |x/scale| * 2^-22 <= 127 * 2^-22 < 2^-14 of the true quotient
 // (|x| <= amax < 127 * scale), so rounding q gives the same integer unless q
 // lies within 2^-14 of a half-integer; only then is the exact quotient used.
-// Rounding is the add of 1.5 * 2^23 (half-to-even in the FPU), and clamping
-// before rounding equals clamping after it because the bounds are integers.
-// Returns the float bits of 1.5 * 2^23 + code: the low byte is the INT8 code.
-__device__ __forceinline__ uint32_t quantize_bits(float x, float scale, float rcp) {
+// Rounding is the add of 1.5 * 2^23 (half-to-even in the FPU).  The clamp
+// never binds: |x/scale| < 127 for finite inputs because scale = amax/127 +
+// 1e-7 exceeds amax/127.  Returns the float bits of 1.5 * 2^23 + code: the
+// low byte is the INT8 code.
+__device__ __forceinline__ uint2 quantize_bits2(float2 x, float scale, float rcp) {
   constexpr float kMagic = 12582912.0f;
-  const float q = fminf(fmaxf(__fmul_rn(x, rcp), -127.0f), 127.0f);
-  float y = __fadd_rn(q, kMagic);
-  if (fabsf(__fsub_rn(q, __fsub_rn(y, kMagic))) > 0.5f - 1.0f / 16384.0f)
-    y = __fadd_rn(fminf(fmaxf(__fdiv_rn(x, scale), -127.0f), 127.0f), kMagic);
-  return __float_as_uint(y);
+  const float2 q = __fmul2_rn(x, make_float2(rcp, rcp));
+  float2 y = __fadd2_rn(q, make_float2(kMagic, kMagic));
+  const float2 r = __fadd2_rn(y, make_float2(-kMagic, -kMagic));
+  const float2 d = __ffma2_rn(r, make_float2(-1.0f, -1.0f), q);
+  constexpr float kNearTie = 0.5f - 1.0f / 16384.0f;
+  if (fabsf(d.x) > kNearTie) y.x = __fadd_rn(fminf(fmaxf(__fdiv_rn(x.x, scale), -127.0f), 127.0f), kMagic);
+  if (fabsf(d.y) > kNearTie) y.y = __fadd_rn(fminf(fmaxf(__fdiv_rn(x.y, scale), -127.0f), 127.0f), kMagic);
+  return make_uint2(__float_as_uint(y.x), __float_as_uint(y.y));
 }
 
 __device__ __forceinline__ float group_scale(float amax) {
@@ -96,6 +86,29 @@ struct PrepassArgs {
   uint8_t* ws;         // workspace base
   piper_b200_workspace_layout_t L;
 };
+
+// ---------------------------------------------------------------------------
+// Raw 16-byte load of 8 consecutive fp16/bf16 elements (element-wise when the
+// address or strides are not 16-byte aligned) and its exact widening.
+template <typename T, bool kVec16>
+__device__ __forceinline__ uint4 load_raw8(const T* p) {
+  if constexpr (kVec16) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+  } else {
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(p);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = static_cast<uint32_t>(e[2 * i]) | (static_cast<uint32_t>(e[2 * i + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& r, float (&out)[8]) {
+  const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = to_f32<T>(e[i]);
+}
 
 // ---------------------------------------------------------------------------
 // Column sums of K (and V when non-causal) over one chunk of rows, in fp64.
@@ -122,13 +135,38 @@ __global__ void __launch_bounds__(kPrepassThreads) kv_sum_kernel(PrepassArgs a) 
 
   const int64_t r0 = static_cast<int64_t>(chunk) * kSumChunkRows;
   const int64_t r1 = min(r0 + kSumChunkRows, a.nk);
-  for (int64_t r = r0 + ro; r < r1; r += kRpp) {
+  // Four rows per step with all their loads issued first, so each thread
+  // keeps 4 (K only) or 8 (K and V) 16-byte loads in flight.
+  constexpr int kUnroll = 4;
+  int64_t r = r0 + ro;
+  for (; r + (kUnroll - 1) * kRpp < r1; r += kUnroll * kRpp) {
+    uint4 rk[kUnroll], rv[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) rk[u] = load_raw8<T, kVec16>(kbase + (r + u * kRpp) * a.ks[2]);
+    if (with_v) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) rv[u] = load_raw8<T, kVec16>(vbase + (r + u * kRpp) * a.vs[2]);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      float x[8];
+      unpack8<T>(rk[u], x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ksum[i] += static_cast<double>(x[i]);
+      if (with_v) {
+        unpack8<T>(rv[u], x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vsum[i] += static_cast<double>(x[i]);
+      }
+    }
+  }
+  for (; r < r1; r += kRpp) {
     float x[8];
-    load8<T, kVec16>(kbase + r * a.ks[2], x);
+    unpack8<T>(load_raw8<T, kVec16>(kbase + r * a.ks[2]), x);
 #pragma unroll
     for (int i = 0; i < 8; ++i) ksum[i] += static_cast<double>(x[i]);
     if (with_v) {
-      load8<T, kVec16>(vbase + r * a.vs[2], x);
+      unpack8<T>(load_raw8<T, kVec16>(vbase + r * a.vs[2]), x);
 #pragma unroll
       for (int i = 0; i < 8; ++i) vsum[i] += static_cast<double>(x[i]);
     }
@@ -202,34 +240,15 @@ __global__ void __launch_bounds__(D) finalize_means_kernel(PrepassArgs a) {
   vmean[bh * D + tid] = a.causal ? 0.0f : static_cast<float>(totals[(bh_all + bh) * D + tid] / n);
 }
 
-// ---------------------------------------------------------------------------
-// Raw 16-byte load of 8 consecutive fp16/bf16 elements (element-wise when the
-// address or strides are not 16-byte aligned) and its exact widening.
-template <typename T, bool kVec16>
-__device__ __forceinline__ uint4 load_raw8(const T* p) {
-  if constexpr (kVec16) {
-    return __ldg(reinterpret_cast<const uint4*>(p));
-  } else {
-    const uint16_t* e = reinterpret_cast<const uint16_t*>(p);
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = static_cast<uint32_t>(e[2 * i]) | (static_cast<uint32_t>(e[2 * i + 1]) << 16);
-    return make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& r, float (&out)[8]) {
-  const T* e = reinterpret_cast<const T*>(&r);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) out[i] = to_f32<T>(e[i]);
-}
-
 // Eight INT8 codes packed into two words (low byte of each code's bits).
 __device__ __forceinline__ uint2 pack_codes(const float (&x)[8], float s, float rs) {
   uint32_t y[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) y[i] = quantize_bits(x[i], s, rs);
+  for (int i = 0; i < 8; i += 2) {
+    const uint2 b = quantize_bits2(make_float2(x[i], x[i + 1]), s, rs);
+    y[i] = b.x;
+    y[i + 1] = b.y;
+  }
   const uint32_t w0 = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
   const uint32_t w1 = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);
   return make_uint2(w0, w1);
