@@ -150,6 +150,22 @@ int piper_b200_attention_shard(void* out, int dtype, int64_t batch, int64_t head
                                const void* workspace, size_t workspace_bytes, const void* kv_pack,
                                float* state, int state_mode, void* stream);
 
+/* piper_b200_attention_shard over a sub-range: query rows
+ * [query_begin, query_begin + query_count) of the query_length rows per head
+ * and keys [key_begin, key_begin + key_count) of the key_length keys of the
+ * K/V pack (both begins multiples of 64).  The workspace, pack, output and
+ * state keep their full shapes; only the range's rows of `out` or of the
+ * state are written.  For causal attention, causal_shift = global position of
+ * query_begin - global position of key_begin.  Used for zig-zag causal rings
+ * and for splitting a problem's keys over several CTAs. */
+int piper_b200_attention_shard_range(void* out, int dtype, int64_t batch, int64_t heads,
+                                     int64_t query_length, int64_t query_begin,
+                                     int64_t query_count, int64_t key_length, int64_t key_begin,
+                                     int64_t key_count, int64_t head_dim, double scale,
+                                     int is_causal, int64_t causal_shift, const void* workspace,
+                                     size_t workspace_bytes, const void* kv_pack, float* state,
+                                     int state_mode, void* stream);
+
 /* Bytes of the per-row state of piper_b200_attention_shard: fp32
  * [B*H, Nq, D] numerators followed by fp32 [B*H, Nq, 2] (max, denominator);
  * 0 for non-positive sizes. */

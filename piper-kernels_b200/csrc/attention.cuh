@@ -101,8 +101,15 @@ struct AttnParams {
   // kStateStore writes that triple back instead of the output.
   int64_t causal_shift;
   int state_mode;
-  float* state_o;   // f32 [B*H, Nq, D]  numerator (bias-free)
-  float* state_ml;  // f32 [B*H, Nq, 2]  (reference max in log2 units, denominator)
+  float* state_o;   // f32 [B*H, nq_all, D]  numerator (bias-free)
+  float* state_ml;  // f32 [B*H, nq_all, 2]  (reference max in log2 units, denominator)
+  // Sub-ranges: this launch covers rows [q_row0, q_row0 + nq) of the nq_all
+  // rows per head (Q codes and scales, output and state are indexed over
+  // nq_all), and keys [k_key0, k_key0 + nk) of the K/V operands (K/V codes,
+  // scales and per-key vectors are laid out for the full key count).
+  // q_row0 and k_key0 are multiples of 64.  One launch over everything has
+  // q_row0 = k_key0 = 0 and nq_all = nq.
+  int64_t nq_all, q_row0, k_key0;
 };
 
 constexpr int kStateLoad = 1;
@@ -316,9 +323,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int t = 0; t < kTiles; ++t)
         if (nb[t] > 0)
           tma_load_3d(sbase + S::kOffQ + t * S::kQBytes, &tmQ, q_full, 0,
-                      static_cast<int>(q0 + t * kTileM), static_cast<int>(bh));
-      const float* vlog2 = p.vlog2 + bh * p.nk_pad;
-      const float* vrcp = p.vrcp + bh * p.nk_pad;
+                      static_cast<int>(p.q_row0 + q0 + t * kTileM), static_cast<int>(bh));
+      const float* vlog2 = p.vlog2 + bh * p.nk_pad + p.k_key0;
+      const float* vrcp = p.vrcp + bh * p.nk_pad + p.k_key0;
+      const int key0 = static_cast<int>(p.k_key0);
       int issued = 0;
       for (int j = 0; j < nb_max; ++j) {
         const int s = j % kStages;
@@ -327,8 +335,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           break;
         const uint32_t fb = kv_full + 8 * (s);
         mbar_arrive_expect_tx(fb, S::kKBytes + S::kVBytes + S::kVecBytes);
-        tma_load_3d(sbase + S::kOffK + s * S::kKBytes, &tmK, fb, 0, j * kKeyBlock, static_cast<int>(bh));
-        tma_load_3d(sbase + S::kOffV + s * S::kVBytes, &tmV, fb, j * kKeyBlock, 0, static_cast<int>(bh));
+        tma_load_3d(sbase + S::kOffK + s * S::kKBytes, &tmK, fb, 0, key0 + j * kKeyBlock, static_cast<int>(bh));
+        tma_load_3d(sbase + S::kOffV + s * S::kVBytes, &tmV, fb, key0 + j * kKeyBlock, 0, static_cast<int>(bh));
         const uint32_t vec = sbase + S::kOffVec + s * S::kVecBytes;
         bulk_load(vec, vlog2 + j * kKeyBlock, kKeyBlock * 4, fb);
         bulk_load(vec + kKeyBlock * 4, vrcp + j * kKeyBlock, kKeyBlock * 4, fb);
@@ -420,13 +428,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = threadIdx.x % kTileM;
     const int row = static_cast<int>(q0) + t * kTileM + r;
     const bool valid_row = row < p.nq;
+    const int64_t grow = p.q_row0 + row;  // row within the head's nq_all rows
     const int nbt = nb[t];
     const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
     const uint32_t tm_s = tmem_base + lane_base + t * 256;
     const uint32_t tm_pv = tm_s + 128;
-    const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + row / kQueryGroup) : 0.0f;
+    const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + grow / kQueryGroup) : 0.0f;
     const float c_row = qs * p.scale_log2e;
-    const float* kscale = p.kscale + bh * p.k_groups;
+    const float* kscale = p.kscale + bh * p.k_groups + p.k_key0 / kKeyGroup;
     const float2 nb2 = make_float2(-kBias, -kBias);
 
     float2 o[D / 2];
@@ -442,14 +451,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if ((p.state_mode & kStateLoad) && valid_row) {
       // Continue the recurrence of earlier key shards: the same identity as
       // a lazy rescale, with the carried reference max.
-      const float4* so = reinterpret_cast<const float4*>(p.state_o + (bh * p.nq + row) * D);
+      const float4* so = reinterpret_cast<const float4*>(p.state_o + (bh * p.nq_all + grow) * D);
 #pragma unroll
       for (int i = 0; i < D / 4; ++i) {
         const float4 v = so[i];
         o[2 * i] = make_float2(v.x, v.y);
         o[2 * i + 1] = make_float2(v.z, v.w);
       }
-      const float2 ml = reinterpret_cast<const float2*>(p.state_ml)[bh * p.nq + row];
+      const float2 ml = reinterpret_cast<const float2*>(p.state_ml)[bh * p.nq_all + grow];
       m_ref = ml.x;
       l_run = ml.y;
     }
@@ -582,16 +591,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bias_acc = fmaf(kBias, pend_w, bias_acc);
 
     if (ok && valid_row && flag_get(abort_flag) == 0 && (p.state_mode & kStateStore)) {
-      float4* so = reinterpret_cast<float4*>(p.state_o + (bh * p.nq + row) * D);
+      float4* so = reinterpret_cast<float4*>(p.state_o + (bh * p.nq_all + grow) * D);
 #pragma unroll
       for (int i = 0; i < D / 4; ++i)
         so[i] = make_float4(o[2 * i].x - bias_acc, o[2 * i].y - bias_acc, o[2 * i + 1].x - bias_acc,
                             o[2 * i + 1].y - bias_acc);
-      reinterpret_cast<float2*>(p.state_ml)[bh * p.nq + row] = make_float2(m_ref, l_run);
+      reinterpret_cast<float2*>(p.state_ml)[bh * p.nq_all + grow] = make_float2(m_ref, l_run);
     } else if (ok && valid_row && flag_get(abort_flag) == 0) {
       const float inv = 1.0f / fmaxf(l_run, 1e-30f);
       const float* vm = p.vmean + bh * D;
-      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq + row) * D);
+      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + grow) * D);
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
         const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);

@@ -214,15 +214,21 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
 
 // The attention launch shared by the one-shot and the sharded entry points:
 // Q side (codes, scales, V mean) from `workspace`, K/V side from `kv_pack`
-// (a K/V pack laid out as in the workspace of the same shape).
-int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
-                  int64_t head_dim, double scale, int is_causal, const void* workspace, size_t workspace_bytes,
-                  const void* kv_pack, int64_t causal_shift, float* state, int state_mode, void* stream,
-                  bool sharded = false) {
+// (a K/V pack laid out as in the workspace of the same shape).  The workspace
+// and pack are for (batch, heads, nq_all, nk_all, head_dim); the launch covers
+// rows [q_row0, q_row0 + q_rows) and keys [key0, key0 + keys).
+int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq_all, int64_t q_row0, int64_t q_rows,
+                  int64_t nk_all, int64_t key0, int64_t keys, int64_t head_dim, double scale, int is_causal,
+                  const void* workspace, size_t workspace_bytes, const void* kv_pack, int64_t causal_shift,
+                  float* state, int state_mode, void* stream, bool sharded = false) {
   // Sharded causal attention pairs independent query and key shards: only the
   // one-shard form needs Nq == Nk.
-  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, sharded ? 0 : is_causal);
+  int rc = check_shape(dtype, batch, heads, nq_all, nk_all, head_dim, sharded ? 0 : is_causal);
   if (rc != PIPER_B200_OK) return rc;
+  if (q_row0 < 0 || q_rows <= 0 || q_row0 + q_rows > nq_all || key0 < 0 || keys <= 0 || key0 + keys > nk_all)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "row or key range outside the problem");
+  if (q_row0 % piper::kKeyBlock != 0 || key0 % piper::kKeyBlock != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "row and key ranges must start at multiples of 64");
   if (!workspace || !kv_pack) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
   if (!(state_mode & piper::kStateStore) && !out) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL output");
   if (state_mode != 0 && !state) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL state");
@@ -237,18 +243,18 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t qu
   int device = 0;
   if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
   const int64_t bh = batch * heads;
-  const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
+  const piper_b200_workspace_layout_t L = piper::make_layout(bh, nq_all, nk_all, head_dim);
   if (workspace_bytes < L.total_bytes)
     return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "workspace too small for this problem");
   const uint8_t* ws = static_cast<const uint8_t*>(workspace);
   const uint8_t* kv = static_cast<const uint8_t*>(kv_pack) - L.kv_pack;  // same offsets as the workspace
   const uint64_t d = static_cast<uint64_t>(head_dim);
   CUtensorMap tmQ, tmK, tmV;
-  if ((rc = encode_map(&tmQ, ws + L.q8, d, query_length, bh, d, query_length * d, static_cast<uint32_t>(d),
-                       piper::kTileM)) != PIPER_B200_OK)
+  if ((rc = encode_map(&tmQ, ws + L.q8, d, nq_all, bh, d, nq_all * d, static_cast<uint32_t>(d), piper::kTileM)) !=
+      PIPER_B200_OK)
     return rc;
-  if ((rc = encode_map(&tmK, kv + L.k8, d, key_length, bh, d, key_length * d, static_cast<uint32_t>(d),
-                       piper::kKeyBlock)) != PIPER_B200_OK)
+  if ((rc = encode_map(&tmK, kv + L.k8, d, nk_all, bh, d, nk_all * d, static_cast<uint32_t>(d), piper::kKeyBlock)) !=
+      PIPER_B200_OK)
     return rc;
   if ((rc = encode_map(&tmV, kv + L.v8t, L.nk_pad, d, bh, L.nk_pad, L.nk_pad * d, piper::kKeyBlock,
                        static_cast<uint32_t>(d))) != PIPER_B200_OK)
@@ -261,19 +267,22 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t qu
   p.vmean = reinterpret_cast<const float*>(ws + L.vmean);
   p.out = out;
   p.heads = heads;
-  p.nq = query_length;
-  p.nk = key_length;
+  p.nq = q_rows;
+  p.nk = keys;
   p.nk_pad = L.nk_pad;
   p.q_groups = L.q_groups;
   p.k_groups = L.k_groups;
   p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
   p.causal = is_causal ? 1 : 0;
-  p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
+  p.q_tiles = static_cast<int>((q_rows + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
   p.wait_budget_ns = piper::kWaitBudgetNs;
   p.causal_shift = causal_shift;
   p.state_mode = state_mode;
   p.state_o = state;
-  p.state_ml = state ? state + bh * query_length * head_dim : nullptr;
+  p.state_ml = state ? state + bh * nq_all * head_dim : nullptr;
+  p.nq_all = nq_all;
+  p.q_row0 = q_row0;
+  p.k_key0 = key0;
   const dim3 grid(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == PIPER_B200_FLOAT16) {
@@ -343,8 +352,9 @@ int piper_b200_attention_prepared(void* out, int dtype, int64_t batch, int64_t h
   int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
   if (rc != PIPER_B200_OK) return rc;
   const piper_b200_workspace_layout_t L = piper::make_layout(batch * heads, query_length, key_length, head_dim);
-  return run_attention(out, dtype, batch, heads, query_length, key_length, head_dim, scale, is_causal, workspace,
-                       workspace_bytes, static_cast<const uint8_t*>(workspace) + L.kv_pack, 0, nullptr, 0, stream);
+  return run_attention(out, dtype, batch, heads, query_length, 0, query_length, key_length, 0, key_length, head_dim,
+                       scale, is_causal, workspace, workspace_bytes, static_cast<const uint8_t*>(workspace) + L.kv_pack,
+                       0, nullptr, 0, stream);
 }
 
 int piper_b200_shard_column_sums(const void* key, const int64_t key_strides[3], const void* value,
@@ -367,18 +377,30 @@ int piper_b200_shard_prepass(const void* query, const int64_t query_strides[3], 
                      kFinalize | kQuantize, 0, total_keys);
 }
 
-int piper_b200_attention_shard(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
-                               int64_t key_length, int64_t head_dim, double scale, int is_causal,
-                               int64_t causal_shift, const void* workspace, size_t workspace_bytes,
-                               const void* kv_pack, float* state, int state_mode, void* stream) {
+int piper_b200_attention_shard_range(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                                     int64_t query_begin, int64_t query_count, int64_t key_length,
+                                     int64_t key_begin, int64_t key_count, int64_t head_dim, double scale,
+                                     int is_causal, int64_t causal_shift, const void* workspace,
+                                     size_t workspace_bytes, const void* kv_pack, float* state, int state_mode,
+                                     void* stream) {
   if (state_mode < 0 || state_mode > (PIPER_B200_STATE_LOAD | PIPER_B200_STATE_STORE))
     return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "state_mode must combine PIPER_B200_STATE_LOAD/STORE");
   if (!is_causal && causal_shift != 0)
     return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "causal_shift applies to causal attention only");
   if (is_causal && (causal_shift < -(int64_t(1) << 40) || causal_shift > (int64_t(1) << 40)))
     return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "causal_shift out of range");
-  return run_attention(out, dtype, batch, heads, query_length, key_length, head_dim, scale, is_causal, workspace,
-                       workspace_bytes, kv_pack, causal_shift, state, state_mode, stream, true);
+  return run_attention(out, dtype, batch, heads, query_length, query_begin, query_count, key_length, key_begin,
+                       key_count, head_dim, scale, is_causal, workspace, workspace_bytes, kv_pack, causal_shift, state,
+                       state_mode, stream, true);
+}
+
+int piper_b200_attention_shard(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                               int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                               int64_t causal_shift, const void* workspace, size_t workspace_bytes,
+                               const void* kv_pack, float* state, int state_mode, void* stream) {
+  return piper_b200_attention_shard_range(out, dtype, batch, heads, query_length, 0, query_length, key_length, 0,
+                                          key_length, head_dim, scale, is_causal, causal_shift, workspace,
+                                          workspace_bytes, kv_pack, state, state_mode, stream);
 }
 
 size_t piper_b200_state_bytes(int64_t batch, int64_t heads, int64_t query_length, int64_t head_dim) {

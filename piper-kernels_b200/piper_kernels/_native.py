@@ -45,6 +45,7 @@ EXPORTED_SYMBOLS = (
     "piper_b200_shard_column_sums",
     "piper_b200_shard_prepass",
     "piper_b200_attention_shard",
+    "piper_b200_attention_shard_range",
     "piper_b200_state_bytes",
     "piper_b200_host_scratch_bytes",
     "piper_b200_attention_fwd_host",
@@ -117,6 +118,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_double, ctypes.c_int, _I64, _VP, ctypes.c_size_t, _VP, _VP, ctypes.c_int, _VP,
     ]
     lib.piper_b200_attention_shard.restype = ctypes.c_int
+    lib.piper_b200_attention_shard_range.argtypes = [_VP, ctypes.c_int] + [_I64] * 9 + [
+        ctypes.c_double, ctypes.c_int, _I64, _VP, ctypes.c_size_t, _VP, _VP, ctypes.c_int, _VP,
+    ]
+    lib.piper_b200_attention_shard_range.restype = ctypes.c_int
     lib.piper_b200_state_bytes.argtypes = [_I64] * 4
     lib.piper_b200_state_bytes.restype = ctypes.c_size_t
     lib.piper_b200_host_scratch_bytes.argtypes = [_I64] * 5 + [ctypes.POINTER(ctypes.c_size_t)]

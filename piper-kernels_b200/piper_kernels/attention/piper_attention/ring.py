@@ -19,8 +19,13 @@ this extends its arithmetic unchanged:
    the next; the last step writes the output.
 
 No output gather is needed: each rank owns its query rows.  Causal
-attention works too (each key shard is placed by ``causal_shift``); with
-contiguous shards its work is unbalanced across ranks.
+attention works with either shard layout (each key range is placed by
+``causal_shift``).  With ``layout="contiguous"`` rank r holds rows
+[r*n, (r+1)*n) and causal work is unbalanced (the last rank sees every key).
+With ``layout="zigzag"`` the sequence is cut into 2*world chunks of n/2 rows
+and rank r holds chunks r and 2*world-1-r (use :func:`zigzag_shard`): every
+rank then has the same causal work, and each ring step runs the attention for
+the (query chunk, key chunk) pairs that are not fully masked.
 
 ``ops_factory`` selects the compute backend; the default is the sm_100a
 library.  Tests substitute a CPU restatement to exercise this host logic over
@@ -63,8 +68,9 @@ class ShardOps(Protocol):
         """Per-row softmax state carried between key shards."""
 
     def attend(self, pack: torch.Tensor, state: torch.Tensor | None, state_mode: int, causal_shift: int,
-               out: torch.Tensor) -> None:
-        """Attention of this shard's queries over the keys in ``pack``."""
+               out: torch.Tensor, query_range: tuple[int, int] | None = None,
+               key_range: tuple[int, int] | None = None) -> None:
+        """Attention of this shard's queries (a row range) over keys in ``pack`` (a key range)."""
 
 
 class NativeShardOps:
@@ -98,10 +104,74 @@ class NativeShardOps:
         b, h, nq, d = self.query.shape
         return torch.empty(b200.state_bytes(b, h, nq, d) // 4, dtype=torch.float32, device=self.query.device)
 
-    def attend(self, pack, state, state_mode, causal_shift, out) -> None:
+    def attend(self, pack, state, state_mode, causal_shift, out, query_range=None, key_range=None) -> None:
         assert self.prepared is not None
         b200.attention_shard(self.prepared, pack, self.scale, state=state, state_mode=state_mode,
-                             causal_shift=causal_shift, out=out)
+                             causal_shift=causal_shift, out=out, query_range=query_range, key_range=key_range)
+
+
+def zigzag_shard(x: torch.Tensor, rank: int, world: int, dim: int = 2) -> torch.Tensor:
+    """Rows of ``x`` (full sequence along ``dim``) that rank ``rank`` holds in the zig-zag layout."""
+    n = x.shape[dim]
+    if n % (2 * world):
+        raise ValueError(f"sequence length {n} does not split into {2 * world} chunks")
+    c = n // (2 * world)
+    first = x.narrow(dim, rank * c, c)
+    second = x.narrow(dim, (2 * world - 1 - rank) * c, c)
+    return torch.cat([first, second], dim=dim)
+
+
+def zigzag_unshard(parts: list[torch.Tensor], dim: int = 2) -> torch.Tensor:
+    """Reassemble the full sequence from every rank's zig-zag shard (rank order)."""
+    world = len(parts)
+    c = parts[0].shape[dim] // 2
+    chunks: list[torch.Tensor | None] = [None] * (2 * world)
+    for r, part in enumerate(parts):
+        chunks[r] = part.narrow(dim, 0, c)
+        chunks[2 * world - 1 - r] = part.narrow(dim, c, c)
+    return torch.cat(chunks, dim=dim)
+
+
+def _plan(rank: int, world: int, n: int, is_causal: bool, layout: str):
+    """Attention launches per ring step: (query_range, key_range, causal_shift, mode).
+
+    The pack held at step s belongs to rank (rank - s) mod world.  Each query
+    range starts its state fresh on its first launch and writes the output on
+    its last.
+    """
+    steps: list[list[list]] = []
+    if layout == "contiguous":
+        for s in range(world):
+            owner = (rank - s) % world
+            shift = (rank - owner) * n if is_causal else 0
+            steps.append([[None, None, shift]])
+    else:
+        c = n // 2
+        chunk_of = lambda r, half: r if half == 0 else 2 * world - 1 - r  # noqa: E731
+        for s in range(world):
+            owner = (rank - s) % world
+            step = []
+            for qh in (0, 1):
+                for kh in (0, 1):
+                    iq, ik = chunk_of(rank, qh), chunk_of(owner, kh)
+                    if is_causal and ik > iq:
+                        continue  # keys entirely after the queries
+                    step.append([(qh * c, c), (kh * c, c), (iq - ik) * c if is_causal else 0])
+            steps.append(step)
+    # State modes: per query range, LOAD after its first launch, STORE before its last.
+    seen: dict = {}
+    total: dict = {}
+    for step in steps:
+        for launch in step:
+            total[launch[0]] = total.get(launch[0], 0) + 1
+    for step in steps:
+        for launch in step:
+            q = launch[0]
+            k = seen.get(q, 0)
+            mode = (STATE_LOAD if k > 0 else 0) | (STATE_STORE if k + 1 < total[q] else 0)
+            seen[q] = k + 1
+            launch.append(mode)
+    return steps
 
 
 def _collective_device(group) -> torch.device:
@@ -131,6 +201,7 @@ def ring_piper_attention(
     scale: float | None = None,
     is_causal: bool = False,
     group: dist.ProcessGroup | None = None,
+    layout: str = "contiguous",
     ops_factory: Callable[..., ShardOps] | None = None,
 ) -> torch.Tensor:
     """Piper Attention of a sequence sharded over ``group`` (this rank's rows).
@@ -141,7 +212,11 @@ def ring_piper_attention(
     equal (up to fp32 rounding in the softmax) to the matching rows of
     ``piper_attention`` on the whole sequence, with identical INT8 codes.
     Without an initialised process group it is ``piper_attention`` on one GPU.
+    ``layout`` is "contiguous" or "zigzag" (see the module docstring; with
+    "zigzag" the shard length must be a multiple of 128).
     """
+    if layout not in ("contiguous", "zigzag"):
+        raise ValueError(f"{OPERATOR} layout must be 'contiguous' or 'zigzag', got {layout!r}")
     distributed = dist.is_available() and dist.is_initialized()
     world = dist.get_world_size(group) if distributed else 1
     rank = dist.get_rank(group) if distributed else 0
@@ -162,9 +237,9 @@ def ring_piper_attention(
             raise ValueError(f"{OPERATOR}: another rank rejected its inputs")
         if not same_shape:
             raise ValueError(f"{OPERATOR} needs the same [B, H, N, D] shard shape on every rank, got {shape} here")
-        if query.shape[2] % SHARD_ALIGNMENT:
-            raise ValueError(f"{OPERATOR} shards must hold a multiple of {SHARD_ALIGNMENT} rows, "
-                             f"got {query.shape[2]}")
+        align = SHARD_ALIGNMENT * (2 if layout == "zigzag" else 1)
+        if query.shape[2] % align:
+            raise ValueError(f"{OPERATOR} shards must hold a multiple of {align} rows, got {query.shape[2]}")
     elif error is not None:
         raise error
     n = key.shape[2]
@@ -183,9 +258,10 @@ def ring_piper_attention(
 
     to_rank = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
     from_rank = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
+    plan = _plan(rank, world, n, is_causal, layout)
     state = ops.new_state()
     receive = [ops.empty_pack() for _ in range(2 if world > 2 else 1)]
-    held, owner = ops.local_pack(), rank
+    held = ops.local_pack()
     for step in range(world):
         last = step + 1 == world
         pending = []
@@ -195,11 +271,13 @@ def ring_piper_attention(
                 dist.P2POp(dist.isend, held, to_rank, group),
                 dist.P2POp(dist.irecv, incoming, from_rank, group),
             ])
-        mode = (STATE_LOAD if step else 0) | (0 if last else STATE_STORE)
-        shift = (rank - owner) * n if is_causal else 0
-        ops.attend(held, state, mode, shift, out)
+        for query_range, key_range, shift, mode in plan[step]:
+            if query_range is None:
+                ops.attend(held, state, mode, shift, out)
+            else:
+                ops.attend(held, state, mode, shift, out, query_range=query_range, key_range=key_range)
         for work in pending:
             work.wait()
         if not last:
-            held, owner = incoming, (owner - 1) % world
+            held = incoming
     return out

@@ -22,6 +22,7 @@ import torch.distributed as dist  # noqa: E402
 
 from piper_kernels import piper_attention  # noqa: E402
 from piper_kernels.attention.piper_attention import ring_piper_attention  # noqa: E402
+from piper_kernels.attention.piper_attention.ring import zigzag_shard  # noqa: E402
 
 
 def main() -> None:
@@ -31,20 +32,28 @@ def main() -> None:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
     try:
-        for is_causal, dtype, n_shard in ((False, torch.bfloat16, 2048), (True, torch.float16, 1024)):
+        cases = ((False, torch.bfloat16, 2048, "contiguous"), (True, torch.float16, 1024, "contiguous"),
+                 (True, torch.bfloat16, 1024, "zigzag"))
+        for is_causal, dtype, n_shard, layout in cases:
             g = torch.Generator(device=dev).manual_seed(123)
             shape = (1, 4, n_shard * world, 128)
             q = torch.randn(shape, generator=g, device=dev).to(dtype)
             k = (torch.randn(shape, generator=g, device=dev) + 1.0).to(dtype)
             v = (torch.randn(shape, generator=g, device=dev) + 0.5).to(dtype)
-            rows = slice(rank * n_shard, (rank + 1) * n_shard)
+            if layout == "zigzag":
+                def mine_of(t):
+                    return zigzag_shard(t, rank, world).contiguous()
+            else:
+                def mine_of(t):
+                    return t[:, :, rank * n_shard : (rank + 1) * n_shard]
             with torch.no_grad():
-                mine = ring_piper_attention(q[:, :, rows], k[:, :, rows], v[:, :, rows], is_causal=is_causal)
-                whole = piper_attention(q, k, v, is_causal=is_causal)[:, :, rows]
+                mine = ring_piper_attention(mine_of(q), mine_of(k), mine_of(v), is_causal=is_causal, layout=layout)
+                whole = mine_of(piper_attention(q, k, v, is_causal=is_causal))
             torch.cuda.synchronize()
             err = (mine.float() - whole.float()).abs()
             if not (err.max().item() < 0.02 and err.mean().item() < 2e-4):
-                raise AssertionError(f"rank {rank} causal={is_causal}: max {err.max().item()} mean {err.mean().item()}")
+                raise AssertionError(f"rank {rank} causal={is_causal} {layout}: max {err.max().item()} "
+                                     f"mean {err.mean().item()}")
         dist.barrier(device_ids=[local])
         print("RING_OK", rank, flush=True)
     finally:

@@ -24,6 +24,7 @@ from conftest import require_b200
 from oracle import oracle
 from piper_kernels import _native, piper_attention
 from piper_kernels.attention.piper_attention import b200, ring_piper_attention
+from piper_kernels.attention.piper_attention.ring import _plan, zigzag_shard
 
 pytestmark = pytest.mark.gpu
 
@@ -61,6 +62,74 @@ def _emulated_ring(q, k, v, world: int, is_causal: bool):
                                  causal_shift=(r - owner) * n if is_causal else 0, out=out)
         outs.append(out)
     return outs, prepared
+
+
+def _emulated_zigzag_ring(q, k, v, world: int, is_causal: bool):
+    """The zig-zag layout through the range entry point, every rank on one GPU."""
+    shards = [tuple(zigzag_shard(t, r, world).contiguous() for t in (q, k, v)) for r in range(world)]
+    n = shards[0][0].shape[2]
+    prepared = [b200.shard_column_sums(*sh, is_causal) for sh in shards]
+    totals = sum(p.column_totals for p in prepared)
+    for p, sh in zip(prepared, shards):
+        p.column_totals.copy_(totals)
+        b200.shard_prepass(*sh, p, total_keys=n * world)
+    scale = q.shape[-1] ** -0.5
+    outs = []
+    for r in range(world):
+        b_, h_, _, d_ = shards[r][0].shape
+        state = torch.empty(b200.state_bytes(b_, h_, n, d_) // 4, dtype=torch.float32, device=q.device)
+        out = torch.empty_like(shards[r][0])
+        for step, launches in enumerate(_plan(r, world, n, is_causal, "zigzag")):
+            owner = (r - step) % world
+            for q_range, k_range, shift, mode in launches:
+                b200.attention_shard(prepared[r], prepared[owner].kv_pack, scale, state=state, state_mode=mode,
+                                     causal_shift=shift, out=out, query_range=q_range, key_range=k_range)
+        outs.append(out)
+    return outs
+
+
+@pytest.mark.parametrize(("world", "n", "dtype", "is_causal"), [
+    (2, 512, torch.bfloat16, True),
+    (4, 256, torch.float16, True),
+    (3, 384, torch.bfloat16, False),
+])
+def test_zigzag_ring_matches_one_shot(world, n, dtype, is_causal) -> None:
+    dev = require_b200()
+    q, k, v = _inputs(world * n, 128, dtype, seed=world * 77 + n)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    with torch.no_grad():
+        outs = _emulated_zigzag_ring(qd, kd, vd, world, is_causal)
+        shot = piper_attention(qd, kd, vd, is_causal=is_causal)
+    torch.cuda.synchronize()
+    assert _native.device_status(0) == 0
+    for r, out in enumerate(outs):
+        err = (out.float() - zigzag_shard(shot, r, world).float()).abs()
+        assert err.max().item() < 0.02 and err.mean().item() < 2e-4, (r, err.max().item(), err.mean().item())
+
+
+def test_key_range_split_with_state_equals_one_launch() -> None:
+    # One shard's keys split into three ranges (split-KV), state carried.
+    dev = require_b200()
+    q, k, v = _inputs(1024, 128, torch.bfloat16, seed=11)
+    qd, kd, vd = (t.to(dev) for t in (q, k, v))
+    with torch.no_grad():
+        p = b200.prepare_piper_attention(qd, kd, vd, False)
+        whole = b200.launch_piper_attention(p, 128**-0.5)
+        state = torch.empty(b200.state_bytes(2, 2, 1024, 128) // 4, dtype=torch.float32, device=dev)
+        out = torch.empty_like(qd)
+        for i, (k0, kn) in enumerate([(0, 320), (320, 448), (768, 256)]):
+            mode = (_native.STATE_LOAD if i else 0) | (_native.STATE_STORE if i < 2 else 0)
+            b200.attention_shard(p, p.kv_pack, 128**-0.5, state=state, state_mode=mode, out=out,
+                                 key_range=(k0, kn), query_range=(0, 1024))
+        # Rows in two ranges as well: the second half of the rows only.
+        half = torch.zeros_like(qd)
+        b200.attention_shard(p, p.kv_pack, 128**-0.5, out=half, query_range=(512, 512))
+    torch.cuda.synchronize()
+    assert _native.device_status(0) == 0
+    err = (out.float() - whole.float()).abs()
+    assert err.max().item() < 0.02 and err.mean().item() < 2e-4
+    assert torch.equal(half[:, :, 512:], whole[:, :, 512:])
+    assert not half[:, :, :512].any()
 
 
 @pytest.mark.parametrize(("world", "n", "d", "dtype", "is_causal"), [
@@ -166,6 +235,10 @@ def test_shard_entry_points_reject_bad_arguments() -> None:
         b200.attention_shard(p, p.kv_pack, 0.1, state_mode=_native.STATE_LOAD)
     with pytest.raises(ValueError, match="256-byte aligned"):
         b200.attention_shard(p, p.kv_pack[16:], 0.1)
+    with pytest.raises(ValueError, match="multiples of 64"):
+        b200.attention_shard(p, p.kv_pack, 0.1, key_range=(32, 64))
+    with pytest.raises(ValueError, match="outside the problem"):
+        b200.attention_shard(p, p.kv_pack, 0.1, query_range=(64, 128))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,

@@ -22,7 +22,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from oracle import oracle
-from piper_kernels.attention.piper_attention.ring import ring_piper_attention
+from piper_kernels.attention.piper_attention.ring import _plan, ring_piper_attention, zigzag_shard, zigzag_unshard
 
 
 class OracleShardOps:
@@ -75,16 +75,37 @@ class OracleShardOps:
     def new_state(self):
         return torch.zeros(self.b * self.h * self.n * (self.d + 2), dtype=torch.float32)
 
-    def attend(self, pack, state, state_mode, causal_shift, out):
+    def attend(self, pack, state, state_mode, causal_shift, out, query_range=None, key_range=None):
+        q0, qn = query_range if query_range is not None else (0, self.n)
+        k0, kn = key_range if key_range is not None else (0, self.n)
+        assert q0 % 64 == 0 and k0 % 64 == 0
+        keys = self._unpack(pack)
+        p = self.prepared
+        query_side = SimpleNamespace(
+            query_int8=np.ascontiguousarray(p.query_int8[:, :, q0 : q0 + qn]),
+            query_scale=np.ascontiguousarray(p.query_scale[:, :, q0 // 32 : (q0 + qn + 31) // 32]),
+            value_mean=p.value_mean,
+        )
+        key_side = SimpleNamespace(
+            key_int8=np.ascontiguousarray(keys.key_int8[:, :, k0 : k0 + kn]),
+            key_scale=np.ascontiguousarray(keys.key_scale[:, :, k0 // 64 : (k0 + kn + 63) // 64]),
+            value_int8=np.ascontiguousarray(keys.value_int8[:, :, k0 : k0 + kn]),
+            value_scale=np.ascontiguousarray(keys.value_scale[:, :, k0 : k0 + kn]),
+        )
         pair = None
         if state is not None:
             cut = self.b * self.h * self.n * self.d
             arr = state.numpy()
-            pair = (arr[:cut].reshape(self.b, self.h, self.n, self.d), arr[cut:].reshape(self.b, self.h, self.n, 2))
-        result = oracle.attention_shard(self.prepared, self._unpack(pack), self.scale, self.is_causal,
-                                        causal_shift=causal_shift, state=pair, state_mode=state_mode)
+            so = arr[:cut].reshape(self.b, self.h, self.n, self.d)
+            sml = arr[cut:].reshape(self.b, self.h, self.n, 2)
+            pair = (np.ascontiguousarray(so[:, :, q0 : q0 + qn]), np.ascontiguousarray(sml[:, :, q0 : q0 + qn]))
+        result = oracle.attention_shard(query_side, key_side, self.scale, self.is_causal, causal_shift=causal_shift,
+                                        state=pair, state_mode=state_mode)
+        if pair is not None and state_mode & oracle.STATE_STORE:
+            so[:, :, q0 : q0 + qn] = pair[0]
+            sml[:, :, q0 : q0 + qn] = pair[1]
         if result is not None:
-            out.copy_(torch.from_numpy(result).to(out.dtype))
+            out[:, :, q0 : q0 + qn] = torch.from_numpy(result).to(out.dtype)
 
 
 def _inputs(n_total: int, d: int, dtype):
@@ -101,11 +122,28 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, n_shard: int, d: int, is_causal: bool) -> None:
+def _worker(rank: int, world: int, port: int, n_shard: int, d: int, is_causal: bool, layout: str = "contiguous") -> None:
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         oracle.set_threads(1)
         q, k, v = _inputs(n_shard * world, d, torch.float16)
+        if layout == "zigzag":
+            def part(x):
+                return zigzag_shard(x, rank, world) if torch.is_tensor(x) else \
+                    zigzag_shard(torch.from_numpy(np.ascontiguousarray(x)), rank, world).numpy()
+            with torch.no_grad():
+                out = ring_piper_attention(part(q), part(k), part(v), is_causal=is_causal, layout="zigzag",
+                                           ops_factory=OracleShardOps)
+            full, prepared = oracle.piper_attention(q, k, v, None, is_causal)
+            mine = OracleShardOps.instances[-1].prepared
+            assert np.array_equal(mine.key_int8, part(prepared.key_int8))
+            assert np.array_equal(mine.value_int8, part(prepared.value_int8))
+            assert np.array_equal(mine.query_int8, part(prepared.query_int8))
+            expected = part(torch.from_numpy(full)).to(out.dtype).float()
+            err = (out.float() - expected).abs()
+            assert err.max().item() <= 2e-3 * max(1.0, expected.abs().max().item()), err.max().item()
+            assert (err > 0).float().mean().item() < 1e-3
+            return
         rows = slice(rank * n_shard, (rank + 1) * n_shard)
         with torch.no_grad():
             out = ring_piper_attention(q[:, :, rows], k[:, :, rows], v[:, :, rows], is_causal=is_causal,
@@ -132,6 +170,28 @@ def _worker(rank: int, world: int, port: int, n_shard: int, d: int, is_causal: b
 @pytest.mark.parametrize("is_causal", [False, True])
 def test_ring_matches_one_shot_oracle(world: int, is_causal: bool) -> None:
     mp.spawn(_worker, args=(world, _free_port(), 128, 64, is_causal), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("is_causal", [True, False])
+def test_zigzag_ring_matches_one_shot_oracle(world: int, is_causal: bool) -> None:
+    mp.spawn(_worker, args=(world, _free_port(), 128, 64, is_causal, "zigzag"), nprocs=world, join=True)
+
+
+def test_zigzag_plan_balances_causal_work() -> None:
+    # Work per rank in block-pair units: a full chunk pair counts 1, a
+    # diagonal pair 1/2.  Contiguous shards give rank r work r + 1/2.
+    for world in (2, 4, 8):
+        works = []
+        for r in range(world):
+            w = 0.0
+            for step in _plan(r, world, 256, True, "zigzag"):
+                for _q, _k, shift, _mode in step:
+                    w += 0.5 if shift == 0 else 1.0
+            works.append(w)
+        assert len(set(works)) == 1, works
+        # (2*world)^2 / 2 chunk pairs are visible in all, spread evenly.
+        assert works[0] == 2.0 * world
 
 
 def _mismatch_worker(rank: int, world: int, port: int, case: str) -> None:
@@ -163,6 +223,13 @@ def _mismatch_worker(rank: int, world: int, port: int, case: str) -> None:
 @pytest.mark.parametrize("case", ["shape", "alignment", "dtype"])
 def test_ring_rejects_inputs_on_every_rank(case: str) -> None:
     mp.spawn(_mismatch_worker, args=(2, _free_port(), case), nprocs=2, join=True)
+
+
+def test_zigzag_shard_round_trip() -> None:
+    x = torch.arange(2 * 3 * 24 * 4).reshape(2, 3, 24, 4)
+    parts = [zigzag_shard(x, r, 3) for r in range(3)]
+    assert torch.equal(parts[0][:, :, :4], x[:, :, 0:4]) and torch.equal(parts[0][:, :, 4:], x[:, :, 20:24])
+    assert torch.equal(zigzag_unshard(parts), x)
 
 
 def test_single_process_ring_is_the_one_shot_operator() -> None:
