@@ -49,9 +49,12 @@ WORKLOADS = {
     "c5": (1, 24, 131072, 128, torch.bfloat16, False,
            "piper_attention non-causal sequence-sharded ring B1 H24 N131072 D128 bf16 (BASELINE configs[4]); "
            "V bias ~N(0,1)"),
+    "c5causal": (1, 24, 131072, 128, torch.bfloat16, True,
+                 "piper_attention CAUSAL sequence-sharded ring, zig-zag shards, B1 H24 N131072 D128 bf16 "
+                 "(the c5 shape with the causal mask; not a BASELINE config)"),
 }
 # Workloads whose sequence is split over the ranks (strong scaling, NCCL ring).
-RING_WORKLOADS = {"c5"}
+RING_WORKLOADS = {"c5", "c5causal"}
 METRIC = "piper_attention TOPS (4*B*H*N^2*D/t) at D=128"
 INT8_NOMINAL_TOPS = 4500.0
 
@@ -79,17 +82,25 @@ def make_ring_inputs(name: str, rank: int, world: int, device: torch.device, hea
     """This rank's rows of the seeded full sequence (identical on every rank).
 
     The union over ranks is the same tensor for every world size, so the
-    ring's output rows equal one GPU's (strong scaling).
+    ring's output rows equal one GPU's (strong scaling).  Causal workloads use
+    the zig-zag layout (chunks r and 2*world-1-r), the others contiguous rows.
     """
-    b, h, n, d, dtype, _causal, _ = WORKLOADS[name]
+    from piper_kernels.attention.piper_attention.ring import zigzag_shard
+
+    b, h, n, d, dtype, causal, _ = WORKLOADS[name]
     h = h if heads is None else heads
     g = torch.Generator(device=device).manual_seed(1000)
     shard = n // world
-    rows = slice(rank * shard, (rank + 1) * shard)
+
+    def mine(t):
+        if causal:
+            return zigzag_shard(t, rank, world)
+        return t[:, :, rank * shard : (rank + 1) * shard]
+
     shape = (b, h, n, d)
-    q = torch.randn(shape, generator=g, device=device)[:, :, rows].to(dtype).contiguous()
-    k = torch.randn(shape, generator=g, device=device)[:, :, rows].to(dtype).contiguous()
-    v = torch.randn(shape, generator=g, device=device)[:, :, rows]
+    q = mine(torch.randn(shape, generator=g, device=device)).to(dtype).contiguous()
+    k = mine(torch.randn(shape, generator=g, device=device)).to(dtype).contiguous()
+    v = mine(torch.randn(shape, generator=g, device=device))
     v = (v + torch.randn((b, h, 1, d), generator=g, device=device)).to(dtype).contiguous()
     return q, k, v
 
@@ -438,6 +449,7 @@ def run_ring(args) -> None:
 
     from piper_kernels import _native
     from piper_kernels.attention.piper_attention import b200, ring_piper_attention
+    from piper_kernels.attention.piper_attention.ring import _plan
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -451,7 +463,8 @@ def run_ring(args) -> None:
         options.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev, pg_options=options)
     b, h, n, d, dtype, causal, desc = WORKLOADS[args.workload]
-    if n % (64 * world):
+    layout = "zigzag" if causal else "contiguous"
+    if n % ((128 if causal else 64) * world):
         raise SystemExit(f"N={n} does not split into {world} shards of whole 64-row groups")
     shard = n // world
     q, k, v = make_ring_inputs(args.workload, rank, world, dev)
@@ -472,7 +485,7 @@ def run_ring(args) -> None:
 
     with torch.no_grad():
         for _ in range(args.warmup):
-            ring_piper_attention(q, k, v, is_causal=causal)
+            ring_piper_attention(q, k, v, is_causal=causal, layout=layout)
         barrier()
         if _native.device_status(local) != 0:
             raise RuntimeError("a kernel reported a timed-out wait during warm-up")
@@ -482,26 +495,33 @@ def run_ring(args) -> None:
         with ClockSampler(local) as clocks:
             start.record(stream)
             for _ in range(args.steps):
-                ring_piper_attention(q, k, v, is_causal=causal)
+                ring_piper_attention(q, k, v, is_causal=causal, layout=layout)
             stop.record(stream)
             torch.cuda.synchronize(dev)
         elapsed_ms = max_over_ranks(start.elapsed_time(stop))
 
         # The dominant kernel alone: one middle ring step's launch (state in and
-        # out) over a resident K/V pack of this rank's shard shape.
+        # out) over a resident K/V pack of this rank's shard shape.  For the
+        # zig-zag layout that is one fully visible (query chunk, key chunk) pair.
         prepared = b200.shard_column_sums(q, k, v, causal)
         b200.shard_prepass(q, k, v, prepared, total_keys=n)
         state = torch.empty(b200.state_bytes(b, h, shard, d) // 4, dtype=torch.float32, device=dev)
-        b200.attention_shard(prepared, prepared.kv_pack, scale, state=state, state_mode=_native.STATE_STORE)
         mode = _native.STATE_LOAD | _native.STATE_STORE
+        if causal:
+            launch_rows = shard // 2
+            span = dict(query_range=(launch_rows, launch_rows), key_range=(0, launch_rows), causal_shift=n)
+        else:
+            launch_rows = shard
+            span = {}
+        b200.attention_shard(prepared, prepared.kv_pack, scale, state=state, state_mode=_native.STATE_STORE, **span)
         for _ in range(2):
-            b200.attention_shard(prepared, prepared.kv_pack, scale, state=state, state_mode=mode)
+            b200.attention_shard(prepared, prepared.kv_pack, scale, state=state, state_mode=mode, **span)
         k0 = torch.cuda.Event(enable_timing=True)
         k1 = torch.cuda.Event(enable_timing=True)
         launches = max(3, min(args.steps, 10))
         k0.record(stream)
         for _ in range(launches):
-            b200.attention_shard(prepared, prepared.kv_pack, scale, state=state, state_mode=mode)
+            b200.attention_shard(prepared, prepared.kv_pack, scale, state=state, state_mode=mode, **span)
         k1.record(stream)
         torch.cuda.synchronize(dev)
         attn_ms = max_over_ranks(k0.elapsed_time(k1) / launches)
@@ -518,7 +538,7 @@ def run_ring(args) -> None:
             dq.copy_(hq, non_blocking=True)
             dk.copy_(hk, non_blocking=True)
             dv.copy_(hv, non_blocking=True)
-            o = ring_piper_attention(dq, dk, dv, is_causal=causal)
+            o = ring_piper_attention(dq, dk, dv, is_causal=causal, layout=layout)
             hout.copy_(o, non_blocking=True)
 
         e2e_step()
@@ -536,14 +556,16 @@ def run_ring(args) -> None:
             raise RuntimeError(f"a kernel reported a timed-out wait (status {status:#x})")
 
     ms_per_step = elapsed_ms / args.steps
-    ops_full = attention_ops(b, h, n, n, d)
+    ops_full = attention_ops(b, h, n, n, d)  # the reference's formula (full N^2 even when causal)
+    ops_visible = ops_full * ((n + 1) / (2 * n) if causal else 1.0)
     value = ops_full / (ms_per_step * 1e-3) / 1e12
     measured = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
     bf16_peak = measured.get("bf16_tflops")
     int8_peak = 2.0 * bf16_peak if bf16_peak else 2.0 * 1590.0
     peak_note = "2 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json)" if bf16_peak else "2 x fallback 1.59 PF bf16"
-    ops_launch = attention_ops(b, h, shard, shard, d)
+    ops_launch = attention_ops(b, h, launch_rows, launch_rows, d)
     attn_tops = ops_launch / (attn_ms * 1e-3) / 1e12
+    launches_per_step = sum(len(st) for st in _plan(rank, world, shard, causal, layout)) if world > 1 else 1
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -583,9 +605,11 @@ def run_ring(args) -> None:
                 "traffic": None,
             },
             "ring_overhead": {
-                "attention_ms_per_step": attn_ms * world,
+                "attention_ms_per_step": attn_ms * ops_visible / world / ops_launch,
                 "ms_per_step": ms_per_step,
-                "frac_outside_attention": 1.0 - attn_ms * world / ms_per_step,
+                "frac_outside_attention": 1.0 - attn_ms * ops_visible / world / ops_launch / ms_per_step,
+                "layout": layout,
+                "visible_tops": ops_visible / (ms_per_step * 1e-3) / 1e12,
             },
             "e2e": {
                 "value": ops_full / (e2e_ms * 1e-3) / 1e12,
@@ -594,10 +618,10 @@ def run_ring(args) -> None:
                 "h2d_bytes_per_step": 3 * q.numel() * q.element_size() * world,
                 "d2h_bytes_per_step": q.numel() * q.element_size() * world,
             },
-            "gpu_launches": (3 + world) * args.steps,
+            "gpu_launches": (3 + launches_per_step) * args.steps,
             "clocks": clocks.summary(),
         }
-        if not args.skip_cpu_baseline:
+        if not args.skip_cpu_baseline and not causal:
             line["cpu_baseline"] = {kk: vv for kk, vv in cpu_baseline(args.workload).items() if kk != "seconds_per_sample"}
         print(json.dumps(line), flush=True)
     if world > 1:
