@@ -342,7 +342,8 @@ def run_b200(args) -> None:
         e1.record(stream)
         torch.cuda.synchronize(dev)
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
-        if not torch.equal(hout, out.cpu()):
+        ref_out = out.cpu().float()
+        if ((hout.float() - ref_out).abs() > 1e-3 + ref_out.abs() / 64).any():
             raise RuntimeError("host-to-host output differs from the device-memory operator")
 
         # The same through the device-memory operator with the copies in

@@ -68,6 +68,11 @@ typedef struct piper_b200_workspace_layout_s {
   uint64_t kv_pack, kv_pack_bytes;
   /* fp64 [2, B*H, D]: K then V column sums of a sequence shard. */
   uint64_t totals;
+  /* Optional tail of the workspace: partial states of the split-KV tail
+   * (split_units_max CTAs).  A workspace of only `split_state` bytes is
+   * accepted and runs without the split. */
+  uint64_t split_state;
+  int64_t split_units_max;
 } piper_b200_workspace_layout_t;
 
 /* ABI version of this header (major*100 + minor). */

@@ -110,6 +110,16 @@ struct AttnParams {
   // q_row0 and k_key0 are multiples of 64.  One launch over everything has
   // q_row0 = k_key0 = 0 and nq_all = nq.
   int64_t nq_all, q_row0, k_key0;
+  // Split-KV tail (non-causal launches without state): CTA u < main_units
+  // takes tile u whole; CTA main_units + i takes key range i % splits of tile
+  // main_units + i / splits and writes its partial state (bias-free numerator
+  // [split_units][256][D], then (reference max, denominator)
+  // [split_units][256][2]) to split_state; merge_split_kernel combines them.
+  // Without a tail, splits = 0 and main_units = every tile.
+  int64_t main_units;
+  int splits;
+  int64_t split_units;
+  float* split_state;
 };
 
 constexpr int kStateLoad = 1;
@@ -217,6 +227,26 @@ __device__ __forceinline__ bool fold_pv(float2 (&o)[D / 2], uint32_t full, uint3
   return true;
 }
 
+// Work unit of this CTA: the tile it takes and, for a CTA of the split tail,
+// its key range (split >= 0).  Cheap enough to recompute where needed, so no
+// register carries it across the main loop.
+struct WorkUnit {
+  int64_t unit, tile;
+  int split;
+};
+__device__ __forceinline__ WorkUnit decode_unit(const AttnParams& p) {
+  WorkUnit w;
+  w.unit = static_cast<int64_t>(blockIdx.x) + static_cast<int64_t>(gridDim.x) * blockIdx.y;
+  w.tile = w.unit;
+  w.split = -1;
+  if (w.unit >= p.main_units) {
+    const int64_t u = w.unit - p.main_units;
+    w.tile = p.main_units + u / p.splits;
+    w.split = static_cast<int>(u % p.splits);
+  }
+  return w;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     piper_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -244,11 +274,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int64_t bh = blockIdx.y;
+  // Work unit -> (tile, key range).  Tiles run query-tile fastest.
+  const WorkUnit wu = decode_unit(p);
+  const int split = wu.split;  // >= 0: this CTA is key range `split` of a tail tile
+  const int64_t bh = wu.tile / p.q_tiles;
+  const int qtl = static_cast<int>(wu.tile % p.q_tiles);
   // Causal work grows with the query position: hand out heavy tiles first.
-  const int qt = p.causal ? (p.q_tiles - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+  const int qt = p.causal ? (p.q_tiles - 1 - qtl) : qtl;
   const int64_t q0 = static_cast<int64_t>(qt) * kTileM * kTiles;
-  const int nblocks_all = static_cast<int>((p.nk + kKeyBlock - 1) / kKeyBlock);
+  int64_t key0 = p.k_key0;  // first key of this CTA's range
+  int64_t nk_cta = p.nk;
+  if (split >= 0) {
+    const int64_t blocks = (p.nk + kKeyBlock - 1) / kKeyBlock;
+    const int64_t b0 = blocks * split / p.splits, b1 = blocks * (split + 1) / p.splits;
+    key0 = p.k_key0 + b0 * kKeyBlock;
+    nk_cta = min(p.nk, b1 * kKeyBlock) - b0 * kKeyBlock;
+  }
+  const int nblocks_all = static_cast<int>((nk_cta + kKeyBlock - 1) / kKeyBlock);
   int nb[kTiles];
 #pragma unroll
   for (int t = 0; t < kTiles; ++t) {
@@ -324,9 +366,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (nb[t] > 0)
           tma_load_3d(sbase + S::kOffQ + t * S::kQBytes, &tmQ, q_full, 0,
                       static_cast<int>(p.q_row0 + q0 + t * kTileM), static_cast<int>(bh));
-      const float* vlog2 = p.vlog2 + bh * p.nk_pad + p.k_key0;
-      const float* vrcp = p.vrcp + bh * p.nk_pad + p.k_key0;
-      const int key0 = static_cast<int>(p.k_key0);
+      const float* vlog2 = p.vlog2 + bh * p.nk_pad + key0;
+      const float* vrcp = p.vrcp + bh * p.nk_pad + key0;
       int issued = 0;
       for (int j = 0; j < nb_max; ++j) {
         const int s = j % kStages;
@@ -335,8 +376,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           break;
         const uint32_t fb = kv_full + 8 * (s);
         mbar_arrive_expect_tx(fb, S::kKBytes + S::kVBytes + S::kVecBytes);
-        tma_load_3d(sbase + S::kOffK + s * S::kKBytes, &tmK, fb, 0, key0 + j * kKeyBlock, static_cast<int>(bh));
-        tma_load_3d(sbase + S::kOffV + s * S::kVBytes, &tmV, fb, key0 + j * kKeyBlock, 0, static_cast<int>(bh));
+        tma_load_3d(sbase + S::kOffK + s * S::kKBytes, &tmK, fb, 0, static_cast<int>(key0) + j * kKeyBlock,
+                    static_cast<int>(bh));
+        tma_load_3d(sbase + S::kOffV + s * S::kVBytes, &tmV, fb, static_cast<int>(key0) + j * kKeyBlock, 0,
+                    static_cast<int>(bh));
         const uint32_t vec = sbase + S::kOffVec + s * S::kVecBytes;
         bulk_load(vec, vlog2 + j * kKeyBlock, kKeyBlock * 4, fb);
         bulk_load(vec + kKeyBlock * 4, vrcp + j * kKeyBlock, kKeyBlock * 4, fb);
@@ -435,7 +478,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t tm_pv = tm_s + 128;
     const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + grow / kQueryGroup) : 0.0f;
     const float c_row = qs * p.scale_log2e;
-    const float* kscale = p.kscale + bh * p.k_groups + p.k_key0 / kKeyGroup;
+    const float* kscale = p.kscale + bh * p.k_groups + key0 / kKeyGroup;
     const float2 nb2 = make_float2(-kBias, -kBias);
 
     float2 o[D / 2];
@@ -590,17 +633,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ok = fold_pv<D>(o, pv_full + 8 * (t), pv_free + 8 * (t), nbt - 1, tm_pv, pend_w, lane, budget, status, abort_flag);
     bias_acc = fmaf(kBias, pend_w, bias_acc);
 
-    if (ok && valid_row && flag_get(abort_flag) == 0 && (p.state_mode & kStateStore)) {
-      float4* so = reinterpret_cast<float4*>(p.state_o + (bh * p.nq_all + grow) * D);
+    // Recomputed here rather than kept live through the loop.
+    const WorkUnit we = decode_unit(p);
+    const int64_t bh_e = we.tile / p.q_tiles;
+    const int64_t grow_e = p.q_row0 + row;
+    if (ok && valid_row && flag_get(abort_flag) == 0 && (we.split >= 0 || (p.state_mode & kStateStore))) {
+      float4* so;
+      float2* sml;
+      if (we.split >= 0) {
+        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
+        so = reinterpret_cast<float4*>(p.split_state + slot * D);
+        sml = reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D) + slot;
+      } else {
+        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow_e) * D);
+        sml = reinterpret_cast<float2*>(p.state_ml) + bh_e * p.nq_all + grow_e;
+      }
 #pragma unroll
       for (int i = 0; i < D / 4; ++i)
         so[i] = make_float4(o[2 * i].x - bias_acc, o[2 * i].y - bias_acc, o[2 * i + 1].x - bias_acc,
                             o[2 * i + 1].y - bias_acc);
-      reinterpret_cast<float2*>(p.state_ml)[bh * p.nq_all + grow] = make_float2(m_ref, l_run);
+      *sml = make_float2(m_ref, l_run);
     } else if (ok && valid_row && flag_get(abort_flag) == 0) {
       const float inv = 1.0f / fmaxf(l_run, 1e-30f);
-      const float* vm = p.vmean + bh * D;
-      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + grow) * D);
+      const float* vm = p.vmean + bh_e * D;
+      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow_e) * D);
 #pragma unroll
       for (int c = 0; c < D / 8; ++c) {
         const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);
@@ -621,6 +677,57 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Combines the partial states of the split tail tiles: with M = max_i m_i,
+// out = sum_i O_i 2^(m_i - M) / max(sum_i l_i 2^(m_i - M), 1e-30) + mean_V
+// (the same identity as the lazy rescale).  grid (tail tiles), 256 threads:
+// one query row each.
+template <typename T, int D>
+__global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const AttnParams p) {
+  const int64_t st = blockIdx.x;
+  const int64_t tile = p.main_units + st;
+  const int64_t bh = tile / p.q_tiles;
+  const int64_t row = (tile % p.q_tiles) * (kTileM * kTiles) + threadIdx.x;
+  if (row >= p.nq) return;
+  constexpr int kRows = kTileM * kTiles;
+  const float2* ml = reinterpret_cast<const float2*>(p.split_state + p.split_units * kRows * D);
+  float mx = -INFINITY;
+  for (int i = 0; i < p.splits; ++i) mx = fmaxf(mx, ml[(st * p.splits + i) * kRows + threadIdx.x].x);
+  float l = 0.0f;
+  float w[8];
+  for (int i = 0; i < p.splits; ++i) {
+    const float2 v = ml[(st * p.splits + i) * kRows + threadIdx.x];
+    w[i] = ex2_approx(v.x - mx);
+    l = fmaf(v.y, w[i], l);
+  }
+  const float inv = 1.0f / fmaxf(l, 1e-30f);
+  const float* vm = p.vmean + bh * D;
+  const int64_t grow = p.q_row0 + row;
+  uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + grow) * D);
+#pragma unroll 4
+  for (int c = 0; c < D / 8; ++c) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < p.splits; ++i) {
+      const float4* so = reinterpret_cast<const float4*>(p.split_state + ((st * p.splits + i) * kRows + threadIdx.x) * D);
+      const float4 a = so[2 * c], b = so[2 * c + 1];
+      acc[0] = fmaf(a.x, w[i], acc[0]);
+      acc[1] = fmaf(a.y, w[i], acc[1]);
+      acc[2] = fmaf(a.z, w[i], acc[2]);
+      acc[3] = fmaf(a.w, w[i], acc[3]);
+      acc[4] = fmaf(b.x, w[i], acc[4]);
+      acc[5] = fmaf(b.y, w[i], acc[5]);
+      acc[6] = fmaf(b.z, w[i], acc[6]);
+      acc[7] = fmaf(b.w, w[i], acc[7]);
+    }
+    uint4 pk;
+    pk.x = pack2<T>(fmaf(acc[0], inv, vm[8 * c]), fmaf(acc[1], inv, vm[8 * c + 1]));
+    pk.y = pack2<T>(fmaf(acc[2], inv, vm[8 * c + 2]), fmaf(acc[3], inv, vm[8 * c + 3]));
+    pk.z = pack2<T>(fmaf(acc[4], inv, vm[8 * c + 4]), fmaf(acc[5], inv, vm[8 * c + 5]));
+    pk.w = pack2<T>(fmaf(acc[6], inv, vm[8 * c + 6]), fmaf(acc[7], inv, vm[8 * c + 7]));
+    orow[c] = pk;
   }
 }
 

@@ -20,7 +20,11 @@
 //   ksum    f64   [BH, chunks, D]             per-chunk partial sums of K
 //   vsum    f64   [BH, chunks, D]             per-chunk partial sums of V
 //   counter u32   [BH]                        chunk-completion counters
-// with Nk_pad = roundup(Nk, 64) and chunks = ceil(Nk / kSumChunkRows).
+//   split   f32   [U, 256, D] + [U, 256, 2]   partial states of the split-KV tail
+// with Nk_pad = roundup(Nk, 64), chunks = ceil(Nk / kSumChunkRows) and
+// U = split_units_max = min(kMaxSplitUnits, 8 * BH * ceil(Nq / 256)).
+// Everything before `split` is required; the split region is optional (a
+// workspace that stops at `split` runs without the split tail).
 #pragma once
 
 #include <stddef.h>
@@ -33,6 +37,8 @@ constexpr int kQueryGroup = 32;     // rows per Q scale (per_warp granularity)
 constexpr int kKeyGroup = 64;       // rows per K scale
 constexpr int kKeyBlock = 64;       // keys per online-softmax block (PV block)
 constexpr int kSumChunkRows = 512;  // rows per partial-sum chunk of the mean pass
+constexpr int kMaxSplitUnits = 256;  // split-KV tail CTAs (at most one wave on <= 256 SMs)
+constexpr int kMaxSplits = 8;       // key ranges per tail tile
 
 inline uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
@@ -64,6 +70,9 @@ inline piper_b200_workspace_layout_t make_layout(int64_t bh, int64_t nq, int64_t
   L.ksum = take(static_cast<uint64_t>(bh * L.chunks * d) * 8);
   L.vsum = take(static_cast<uint64_t>(bh * L.chunks * d) * 8);
   L.counter = take(static_cast<uint64_t>(bh) * 4);
+  const int64_t tiles = bh * ((nq + 255) / 256);
+  L.split_units_max = tiles > kMaxSplitUnits / kMaxSplits ? kMaxSplitUnits : tiles * kMaxSplits;
+  L.split_state = take(static_cast<uint64_t>(L.split_units_max) * 256 * (d + 2) * 4);
   L.total_bytes = off;
   return L;
 }

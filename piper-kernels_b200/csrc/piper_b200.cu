@@ -45,6 +45,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 constexpr int kMaxDevices = 64;
 std::mutex g_init_mutex;
 bool g_device_ready[kMaxDevices] = {};
+int g_device_sms[kMaxDevices] = {};
 EncodeTiledFn g_encode = nullptr;
 
 // One-time per-device set-up (thread safe): architecture check and the
@@ -58,6 +59,7 @@ int ensure_device(int* device_out) {
   if (g_device_ready[device]) return PIPER_B200_OK;
   cudaDeviceProp prop;
   PIPER_CUDA(cudaGetDeviceProperties(&prop, device));
+  g_device_sms[device] = prop.multiProcessorCount;
   if (prop.major != 10 || prop.minor != 0)
     return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE,
                 "piper_b200 requires an sm_100 (B200-class) GPU, got sm_" + std::to_string(prop.major) +
@@ -171,9 +173,9 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
   if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
   const int64_t bh = batch * heads;
   const piper_b200_workspace_layout_t L = piper::make_layout(bh, query_length, key_length, head_dim);
-  if (workspace_bytes < L.total_bytes)
+  if (workspace_bytes < L.split_state)
     return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
-                "workspace needs " + std::to_string(L.total_bytes) + " bytes, got " + std::to_string(workspace_bytes));
+                "workspace needs " + std::to_string(L.split_state) + " bytes, got " + std::to_string(workspace_bytes));
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
     return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -244,7 +246,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
   const int64_t bh = batch * heads;
   const piper_b200_workspace_layout_t L = piper::make_layout(bh, nq_all, nk_all, head_dim);
-  if (workspace_bytes < L.total_bytes)
+  if (workspace_bytes < L.split_state)
     return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "workspace too small for this problem");
   const uint8_t* ws = static_cast<const uint8_t*>(workspace);
   const uint8_t* kv = static_cast<const uint8_t*>(kv_pack) - L.kv_pack;  // same offsets as the workspace
@@ -283,18 +285,49 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   p.nq_all = nq_all;
   p.q_row0 = q_row0;
   p.k_key0 = key0;
-  const dim3 grid(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
+  // Work units: every tile whole, except that the tiles of a last partial
+  // wave may be cut into key ranges (split-KV tail) so that the wave ends
+  // sooner; merge_split_kernel then combines their partial states.  Only for
+  // non-causal launches without state, and when the workspace has the
+  // optional split region.
+  const int64_t tiles = static_cast<int64_t>(p.q_tiles) * bh;
+  p.main_units = tiles;
+  p.splits = 0;
+  p.split_units = 0;
+  p.split_state = reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + L.split_state);
+  const int sms = g_device_sms[device] > 0 ? g_device_sms[device] : 148;
+  if (!is_causal && state_mode == 0 && workspace_bytes >= L.total_bytes && tiles < (int64_t(1) << 30)) {
+    const int64_t tail = tiles % sms;
+    const int64_t blocks = (keys + piper::kKeyBlock - 1) / piper::kKeyBlock;
+    const int64_t k = tail > 0 ? std::min<int64_t>({int64_t(piper::kMaxSplits), sms / tail, blocks / 2}) : 0;
+    if (k >= 2 && tail * k <= L.split_units_max) {
+      p.main_units = tiles - tail;
+      p.splits = static_cast<int>(k);
+      p.split_units = tail * k;
+    }
+  }
+  const int64_t units = p.main_units + p.split_units;
+  const dim3 grid = units < (int64_t(1) << 31) ? dim3(static_cast<unsigned>(units), 1)
+                                                : dim3(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 merge_grid(static_cast<unsigned>(p.split_units > 0 ? p.split_units / p.splits : 0));
+  constexpr unsigned kMergeThreads = piper::kTileM * piper::kTiles;
   if (dtype == PIPER_B200_FLOAT16) {
-    if (head_dim == 64)
+    if (head_dim == 64) {
       piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-    else
+      if (p.split_units) piper::merge_split_kernel<__half, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
+    } else {
       piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      if (p.split_units) piper::merge_split_kernel<__half, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
+    }
   } else {
-    if (head_dim == 64)
+    if (head_dim == 64) {
       piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-    else
+      if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
+    } else {
       piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
+    }
   }
   PIPER_CUDA(cudaGetLastError());
   return PIPER_B200_OK;
@@ -304,7 +337,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
 
 extern "C" {
 
-int piper_b200_abi_version(void) { return 101; }
+int piper_b200_abi_version(void) { return 102; }
 
 const char* piper_b200_last_error(void) { return g_last_error.c_str(); }
 
@@ -531,9 +564,9 @@ extern "C" int piper_b200_attention_fwd_no_alloc(const void* query, const int64_
   int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
   if (rc != PIPER_B200_OK) return rc;
   const piper_b200_workspace_layout_t L = piper::make_layout(batch * heads, query_length, key_length, head_dim);
-  if (L.total_bytes > PIPER_B200_NO_ALLOC_WORKSPACE_BYTES)
+  if (L.split_state > PIPER_B200_NO_ALLOC_WORKSPACE_BYTES)
     return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
-                "this problem needs " + std::to_string(L.total_bytes) +
+                "this problem needs " + std::to_string(L.split_state) +
                     " bytes of scratch; piper_b200_attention_fwd_no_alloc holds at most " +
                     std::to_string(PIPER_B200_NO_ALLOC_WORKSPACE_BYTES) +
                     " bytes (use piper_b200_attention_fwd with a caller-provided workspace)");

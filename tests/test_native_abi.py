@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol() -> None:
 
 
 def test_abi_version() -> None:
-    assert _native.library().piper_b200_abi_version() == 101
+    assert _native.library().piper_b200_abi_version() == 102
 
 
 def test_workspace_layout_regions_are_aligned_and_disjoint() -> None:
@@ -45,7 +45,10 @@ def test_workspace_layout_regions_are_aligned_and_disjoint() -> None:
             (L.vscale, bh * L.nk_pad * 4), (L.vlog2, bh * L.nk_pad * 4), (L.vrcp, bh * L.nk_pad * 4),
             (L.kmean, bh * d * 4), (L.vmean, bh * d * 4), (L.totals, 2 * bh * d * 8),
             (L.ksum, bh * L.chunks * d * 8), (L.vsum, bh * L.chunks * d * 8), (L.counter, bh * 4),
+            (L.split_state, L.split_units_max * 256 * (d + 2) * 4),
         ]
+        tiles = bh * -(-nq // 256)
+        assert L.split_units_max == min(256, 8 * tiles)
         # The K/V pack is the contiguous span from the K codes to the end of vrcp.
         assert L.kv_pack == L.k8
         assert L.vrcp + bh * L.nk_pad * 4 <= L.kv_pack + L.kv_pack_bytes <= L.kmean
