@@ -110,11 +110,13 @@ struct AttnParams {
   // q_row0 and k_key0 are multiples of 64.  One launch over everything has
   // q_row0 = k_key0 = 0 and nq_all = nq.
   int64_t nq_all, q_row0, k_key0;
-  // Split-KV tail (non-causal launches without state): CTA u < main_units
+  // Split-KV tail (non-causal launches): CTA u < main_units
   // takes tile u whole; CTA main_units + i takes key range i % splits of tile
   // main_units + i / splits and writes its partial state (bias-free numerator
   // [split_units][256][D], then (reference max, denominator)
-  // [split_units][256][2]) to split_state; merge_split_kernel combines them.
+  // [split_units][256][2]) to split_state; merge_split_kernel combines them
+  // (key range 0 starts from the carried state under kStateLoad) and writes
+  // the output, or the state under kStateStore.
   // Without a tail, splits = 0 and main_units = every tile.
   int64_t main_units;
   int splits;
@@ -491,7 +493,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float pend_w = 0.0f;  // weight of the PV block awaiting its fold
     float bias_acc = 0.0f;  // o holds numerator + bias_acc (same FMAs with PV = 0)
     bool ok = true;
-    if ((p.state_mode & kStateLoad) && valid_row) {
+    // In a split tile only key range 0 continues from the carried state; the
+    // merge combines the ranges.
+    if ((p.state_mode & kStateLoad) && valid_row && split <= 0) {
       // Continue the recurrence of earlier key shards: the same identity as
       // a lazy rescale, with the carried reference max.
       const float4* so = reinterpret_cast<const float4*>(p.state_o + (bh * p.nq_all + grow) * D);
@@ -683,8 +687,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // ---------------------------------------------------------------------------
 // Combines the partial states of the split tail tiles: with M = max_i m_i,
 // out = sum_i O_i 2^(m_i - M) / max(sum_i l_i 2^(m_i - M), 1e-30) + mean_V
-// (the same identity as the lazy rescale).  grid (tail tiles), 256 threads:
-// one query row each.
+// (the same identity as the lazy rescale), or under kStateStore the merged
+// state (sum_i O_i 2^(m_i - M), M, sum_i l_i 2^(m_i - M)).  grid (tail
+// tiles), 256 threads: one query row each.
 template <typename T, int D>
 __global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const AttnParams p) {
   const int64_t st = blockIdx.x;
@@ -697,16 +702,18 @@ __global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const Attn
   float mx = -INFINITY;
   for (int i = 0; i < p.splits; ++i) mx = fmaxf(mx, ml[(st * p.splits + i) * kRows + threadIdx.x].x);
   float l = 0.0f;
-  float w[8];
+  float w[kMaxSplits];
   for (int i = 0; i < p.splits; ++i) {
     const float2 v = ml[(st * p.splits + i) * kRows + threadIdx.x];
     w[i] = ex2_approx(v.x - mx);
     l = fmaf(v.y, w[i], l);
   }
+  const bool store = (p.state_mode & kStateStore) != 0;
   const float inv = 1.0f / fmaxf(l, 1e-30f);
   const float* vm = p.vmean + bh * D;
   const int64_t grow = p.q_row0 + row;
   uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + grow) * D);
+  float4* srow = reinterpret_cast<float4*>(p.state_o + (bh * p.nq_all + grow) * D);
 #pragma unroll 4
   for (int c = 0; c < D / 8; ++c) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -722,13 +729,19 @@ __global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const Attn
       acc[6] = fmaf(b.z, w[i], acc[6]);
       acc[7] = fmaf(b.w, w[i], acc[7]);
     }
-    uint4 pk;
-    pk.x = pack2<T>(fmaf(acc[0], inv, vm[8 * c]), fmaf(acc[1], inv, vm[8 * c + 1]));
-    pk.y = pack2<T>(fmaf(acc[2], inv, vm[8 * c + 2]), fmaf(acc[3], inv, vm[8 * c + 3]));
-    pk.z = pack2<T>(fmaf(acc[4], inv, vm[8 * c + 4]), fmaf(acc[5], inv, vm[8 * c + 5]));
-    pk.w = pack2<T>(fmaf(acc[6], inv, vm[8 * c + 6]), fmaf(acc[7], inv, vm[8 * c + 7]));
-    orow[c] = pk;
+    if (store) {
+      srow[2 * c] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      srow[2 * c + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 pk;
+      pk.x = pack2<T>(fmaf(acc[0], inv, vm[8 * c]), fmaf(acc[1], inv, vm[8 * c + 1]));
+      pk.y = pack2<T>(fmaf(acc[2], inv, vm[8 * c + 2]), fmaf(acc[3], inv, vm[8 * c + 3]));
+      pk.z = pack2<T>(fmaf(acc[4], inv, vm[8 * c + 4]), fmaf(acc[5], inv, vm[8 * c + 5]));
+      pk.w = pack2<T>(fmaf(acc[6], inv, vm[8 * c + 6]), fmaf(acc[7], inv, vm[8 * c + 7]));
+      orow[c] = pk;
+    }
   }
+  if (store) reinterpret_cast<float2*>(p.state_ml)[bh * p.nq_all + grow] = make_float2(mx, l);
 }
 
 // ---------------------------------------------------------------------------

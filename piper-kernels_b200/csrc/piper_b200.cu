@@ -287,16 +287,16 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   p.k_key0 = key0;
   // Work units: every tile whole, except that the tiles of a last partial
   // wave may be cut into key ranges (split-KV tail) so that the wave ends
-  // sooner; merge_split_kernel then combines their partial states.  Only for
-  // non-causal launches without state, and when the workspace has the
-  // optional split region.
+  // sooner; merge_split_kernel then combines their partial states (and the
+  // carried state, which key range 0 starts from).  Only for non-causal
+  // launches, and when the workspace has the optional split region.
   const int64_t tiles = static_cast<int64_t>(p.q_tiles) * bh;
   p.main_units = tiles;
   p.splits = 0;
   p.split_units = 0;
   p.split_state = reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + L.split_state);
   const int sms = g_device_sms[device] > 0 ? g_device_sms[device] : 148;
-  if (!is_causal && state_mode == 0 && workspace_bytes >= L.total_bytes && tiles < (int64_t(1) << 30)) {
+  if (!is_causal && workspace_bytes >= L.total_bytes && tiles < (int64_t(1) << 30)) {
     const int64_t tail = tiles % sms;
     const int64_t blocks = (keys + piper::kKeyBlock - 1) / piper::kKeyBlock;
     const int64_t k = tail > 0 ? std::min<int64_t>({int64_t(piper::kMaxSplits), sms / tail, blocks / 2}) : 0;
