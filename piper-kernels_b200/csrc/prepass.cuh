@@ -48,26 +48,20 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
 }
 
 // clamp(round_half_even(x / scale), -127, 127), bit-exact with the IEEE
-// quotient, without a division or a float-to-int conversion per element,
-// for a pair of elements at a time (packed f32x2 arithmetic).
+// quotient, without a division or a float-to-int conversion per element.
 // q = x * (1/scale) (reciprocal correctly rounded) is within
 // |x/scale| * 2^-22 <= 127 * 2^-22 < 2^-14 of the true quotient
 // (|x| <= amax < 127 * scale), so rounding q gives the same integer unless q
 // lies within 2^-14 of a half-integer; only then is the exact quotient used.
-// Rounding is the add of 1.5 * 2^23 (half-to-even in the FPU).  The clamp
-// never binds: |x/scale| < 127 for finite inputs because scale = amax/127 +
-// 1e-7 exceeds amax/127.  Returns the float bits of 1.5 * 2^23 + code: the
-// low byte is the INT8 code.
-__device__ __forceinline__ uint2 quantize_bits2(float2 x, float scale, float rcp) {
-  constexpr float kMagic = 12582912.0f;
-  const float2 q = __fmul2_rn(x, make_float2(rcp, rcp));
-  float2 y = __fadd2_rn(q, make_float2(kMagic, kMagic));
-  const float2 r = __fadd2_rn(y, make_float2(-kMagic, -kMagic));
-  const float2 d = __ffma2_rn(r, make_float2(-1.0f, -1.0f), q);
-  constexpr float kNearTie = 0.5f - 1.0f / 16384.0f;
-  if (fabsf(d.x) > kNearTie) y.x = __fadd_rn(fminf(fmaxf(__fdiv_rn(x.x, scale), -127.0f), 127.0f), kMagic);
-  if (fabsf(d.y) > kNearTie) y.y = __fadd_rn(fminf(fmaxf(__fdiv_rn(x.y, scale), -127.0f), 127.0f), kMagic);
-  return make_uint2(__float_as_uint(y.x), __float_as_uint(y.y));
+// Rounding is the add of 1.5 * 2^23 (half-to-even in the FPU); the code is
+// the low byte of the sum's bits.  The clamp never binds for the fast path:
+// |x/scale| < 127 for finite inputs because scale = amax/127 + 1e-7 exceeds
+// amax/127.
+constexpr float kMagic = 12582912.0f;
+constexpr float kNearTie = 0.5f - 1.0f / 16384.0f;
+
+__device__ __forceinline__ uint32_t exact_code_bits(float x, float scale) {
+  return __float_as_uint(__fadd_rn(fminf(fmaxf(__fdiv_rn(x, scale), -127.0f), 127.0f), kMagic));
 }
 
 __device__ __forceinline__ float group_scale(float amax) {
@@ -240,14 +234,30 @@ __global__ void __launch_bounds__(D) finalize_means_kernel(PrepassArgs a) {
   vmean[bh * D + tid] = a.causal ? 0.0f : static_cast<float>(totals[(bh_all + bh) * D + tid] / n);
 }
 
-// Eight INT8 codes packed into two words (low byte of each code's bits).
+// Eight INT8 codes packed into two words, computed in packed f32x2
+// arithmetic.  The near-tie test of all eight feeds one vote over the active
+// lanes, so the exact-division fallback is a real branch that warps skip
+// unless one of their lanes has a near-tie (it is never issued predicated
+// off for every element).
 __device__ __forceinline__ uint2 pack_codes(const float (&x)[8], float s, float rs) {
   uint32_t y[8];
+  bool near = false;
 #pragma unroll
   for (int i = 0; i < 8; i += 2) {
-    const uint2 b = quantize_bits2(make_float2(x[i], x[i + 1]), s, rs);
-    y[i] = b.x;
-    y[i + 1] = b.y;
+    const float2 q = __fmul2_rn(make_float2(x[i], x[i + 1]), make_float2(rs, rs));
+    const float2 t = __fadd2_rn(q, make_float2(kMagic, kMagic));
+    const float2 r = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+    const float2 d = __ffma2_rn(r, make_float2(-1.0f, -1.0f), q);
+    near |= (fabsf(d.x) > kNearTie) | (fabsf(d.y) > kNearTie);
+    y[i] = __float_as_uint(t.x);
+    y[i + 1] = __float_as_uint(t.y);
+  }
+  if (__any_sync(__activemask(), near)) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float q = __fmul_rn(x[i], rs);
+      if (fabsf(__fsub_rn(q, __fsub_rn(__fadd_rn(q, kMagic), kMagic))) > kNearTie) y[i] = exact_code_bits(x[i], s);
+    }
   }
   const uint32_t w0 = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
   const uint32_t w1 = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);
