@@ -328,6 +328,7 @@ def attention_shard(
     out: torch.Tensor | None = None,
     query_range: tuple[int, int] | None = None,
     key_range: tuple[int, int] | None = None,
+    masked: bool | None = None,
 ) -> torch.Tensor | None:
     """Attention of this shard's queries over one shard of keys (a K/V pack).
 
@@ -335,14 +336,18 @@ def attention_shard(
     state between key shards; see ``piper_b200_attention_shard``.
     ``query_range`` / ``key_range`` = (begin, count) restrict the launch to
     those query rows and keys (begins multiples of 64); the output and state
-    keep their full shapes.  Returns the output unless ``state_mode`` stores
-    the state instead.
+    keep their full shapes.  ``masked=False`` runs a causal problem's launch
+    without the causal mask, for keys that all precede the queries (the V
+    mean of a causal prepass is already zero).  Returns the output unless
+    ``state_mode`` stores the state instead.
     """
     lib = _native.library()
     b, h, nq, nk, d = prepared.shape
     nk = nk if key_length is None else int(key_length)
     q0, qn = query_range if query_range is not None else (0, nq)
     k0, kn = key_range if key_range is not None else (0, nk)
+    unmasked = masked is False  # an explicit request to drop the causal mask
+    causal = prepared.is_causal and not unmasked
     device = prepared.workspace.device
     if out is None and not state_mode & _native.STATE_STORE:
         out = torch.empty((b, h, nq, d), dtype=prepared.dtype, device=device)
@@ -350,7 +355,7 @@ def attention_shard(
         _native.check(
             lib.piper_b200_attention_shard_range(
                 None if out is None else _ptr(out), _DTYPE_CODES[prepared.dtype], b, h, nq, int(q0), int(qn), nk,
-                int(k0), int(kn), d, float(scale), 1 if prepared.is_causal else 0, int(causal_shift),
+                int(k0), int(kn), d, float(scale), 1 if causal else 0, 0 if unmasked else int(causal_shift),
                 _ptr(prepared.workspace), prepared.workspace.numel(), _ptr(kv_pack),
                 None if state is None else _ptr(state), int(state_mode), _stream(device),
             ),

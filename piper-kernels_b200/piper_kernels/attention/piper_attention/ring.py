@@ -69,8 +69,12 @@ class ShardOps(Protocol):
 
     def attend(self, pack: torch.Tensor, state: torch.Tensor | None, state_mode: int, causal_shift: int,
                out: torch.Tensor, query_range: tuple[int, int] | None = None,
-               key_range: tuple[int, int] | None = None) -> None:
-        """Attention of this shard's queries (a row range) over keys in ``pack`` (a key range)."""
+               key_range: tuple[int, int] | None = None, masked: bool | None = None) -> None:
+        """Attention of this shard's queries (a row range) over keys in ``pack`` (a key range).
+
+        ``masked=False`` runs a causal problem's launch without the mask (its
+        keys all precede its queries).
+        """
 
 
 class NativeShardOps:
@@ -104,10 +108,12 @@ class NativeShardOps:
         b, h, nq, d = self.query.shape
         return torch.empty(b200.state_bytes(b, h, nq, d) // 4, dtype=torch.float32, device=self.query.device)
 
-    def attend(self, pack, state, state_mode, causal_shift, out, query_range=None, key_range=None) -> None:
+    def attend(self, pack, state, state_mode, causal_shift, out, query_range=None, key_range=None,
+               masked=None) -> None:
         assert self.prepared is not None
         b200.attention_shard(self.prepared, pack, self.scale, state=state, state_mode=state_mode,
-                             causal_shift=causal_shift, out=out, query_range=query_range, key_range=key_range)
+                             causal_shift=causal_shift, out=out, query_range=query_range, key_range=key_range,
+                             masked=masked)
 
 
 def zigzag_shard(x: torch.Tensor, rank: int, world: int, dim: int = 2) -> torch.Tensor:
@@ -133,18 +139,20 @@ def zigzag_unshard(parts: list[torch.Tensor], dim: int = 2) -> torch.Tensor:
 
 
 def _plan(rank: int, world: int, n: int, is_causal: bool, layout: str):
-    """Attention launches per ring step: (query_range, key_range, causal_shift, mode).
+    """Attention launches per ring step: (query_range, key_range, causal_shift, mode, masked).
 
     The pack held at step s belongs to rank (rank - s) mod world.  Each query
     range starts its state fresh on its first launch and writes the output on
-    its last.
+    its last.  A causal launch whose keys all precede its queries needs no
+    mask (masked=False), which lets it use the non-causal kernel path (and its
+    split-KV tail).
     """
     steps: list[list[list]] = []
     if layout == "contiguous":
         for s in range(world):
             owner = (rank - s) % world
             shift = (rank - owner) * n if is_causal else 0
-            steps.append([[None, None, shift]])
+            steps.append([[None, None, shift, is_causal and owner >= rank]])
     else:
         c = n // 2
         chunk_of = lambda r, half: r if half == 0 else 2 * world - 1 - r  # noqa: E731
@@ -156,7 +164,7 @@ def _plan(rank: int, world: int, n: int, is_causal: bool, layout: str):
                     iq, ik = chunk_of(rank, qh), chunk_of(owner, kh)
                     if is_causal and ik > iq:
                         continue  # keys entirely after the queries
-                    step.append([(qh * c, c), (kh * c, c), (iq - ik) * c if is_causal else 0])
+                    step.append([(qh * c, c), (kh * c, c), (iq - ik) * c if is_causal else 0, is_causal and ik == iq])
             steps.append(step)
     # State modes: per query range, LOAD after its first launch, STORE before its last.
     seen: dict = {}
@@ -170,7 +178,7 @@ def _plan(rank: int, world: int, n: int, is_causal: bool, layout: str):
             k = seen.get(q, 0)
             mode = (STATE_LOAD if k > 0 else 0) | (STATE_STORE if k + 1 < total[q] else 0)
             seen[q] = k + 1
-            launch.append(mode)
+            launch.insert(3, mode)
     return steps
 
 
@@ -271,11 +279,9 @@ def ring_piper_attention(
                 dist.P2POp(dist.isend, held, to_rank, group),
                 dist.P2POp(dist.irecv, incoming, from_rank, group),
             ])
-        for query_range, key_range, shift, mode in plan[step]:
-            if query_range is None:
-                ops.attend(held, state, mode, shift, out)
-            else:
-                ops.attend(held, state, mode, shift, out, query_range=query_range, key_range=key_range)
+        for query_range, key_range, shift, mode, masked in plan[step]:
+            ops.attend(held, state, mode, shift if masked else 0, out, query_range=query_range, key_range=key_range,
+                       masked=masked)
         for work in pending:
             work.wait()
         if not last:

@@ -81,9 +81,10 @@ def _emulated_zigzag_ring(q, k, v, world: int, is_causal: bool):
         out = torch.empty_like(shards[r][0])
         for step, launches in enumerate(_plan(r, world, n, is_causal, "zigzag")):
             owner = (r - step) % world
-            for q_range, k_range, shift, mode in launches:
+            for q_range, k_range, shift, mode, masked in launches:
                 b200.attention_shard(prepared[r], prepared[owner].kv_pack, scale, state=state, state_mode=mode,
-                                     causal_shift=shift, out=out, query_range=q_range, key_range=k_range)
+                                     causal_shift=shift, out=out, query_range=q_range, key_range=k_range,
+                                     masked=masked)
         outs.append(out)
     return outs
 

@@ -75,7 +75,7 @@ class OracleShardOps:
     def new_state(self):
         return torch.zeros(self.b * self.h * self.n * (self.d + 2), dtype=torch.float32)
 
-    def attend(self, pack, state, state_mode, causal_shift, out, query_range=None, key_range=None):
+    def attend(self, pack, state, state_mode, causal_shift, out, query_range=None, key_range=None, masked=None):
         q0, qn = query_range if query_range is not None else (0, self.n)
         k0, kn = key_range if key_range is not None else (0, self.n)
         assert q0 % 64 == 0 and k0 % 64 == 0
@@ -99,7 +99,8 @@ class OracleShardOps:
             so = arr[:cut].reshape(self.b, self.h, self.n, self.d)
             sml = arr[cut:].reshape(self.b, self.h, self.n, 2)
             pair = (np.ascontiguousarray(so[:, :, q0 : q0 + qn]), np.ascontiguousarray(sml[:, :, q0 : q0 + qn]))
-        result = oracle.attention_shard(query_side, key_side, self.scale, self.is_causal, causal_shift=causal_shift,
+        causal = self.is_causal if masked is None else (self.is_causal and masked)
+        result = oracle.attention_shard(query_side, key_side, self.scale, causal, causal_shift=causal_shift,
                                         state=pair, state_mode=state_mode)
         if pair is not None and state_mode & oracle.STATE_STORE:
             so[:, :, q0 : q0 + qn] = pair[0]
@@ -186,7 +187,8 @@ def test_zigzag_plan_balances_causal_work() -> None:
         for r in range(world):
             w = 0.0
             for step in _plan(r, world, 256, True, "zigzag"):
-                for _q, _k, shift, _mode in step:
+                for _q, _k, shift, _mode, masked in step:
+                    assert masked == (shift == 0)  # only diagonal pairs need the mask
                     w += 0.5 if shift == 0 else 1.0
             works.append(w)
         assert len(set(works)) == 1, works
