@@ -186,3 +186,17 @@ def test_split_tail_matches_unsplit_launch(shape, dtype) -> None:
     err = (split.float() - unsplit.float()).abs()
     assert err.max().item() < 0.02 and err.mean().item() < 2e-4
     _compare(split, oracle.piper_attention_torch(q.cpu(), k.cpu(), v.cpu(), d**-0.5, False))
+
+
+def test_benchmark_record_through_the_gpu() -> None:
+    from piper_kernels import benchmarking as bm
+
+    dev = require_b200()
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn((1, 4, 1024, 128), generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    rec = bm.measure_piper_attention(q, k, v, warmup_ms=5, measurement_time_ms=20).as_dict()
+    t = rec["timings"]
+    assert t["prepared_execution"]["clock"] == bm.DEVICE_EVENT and t["preparation"]["clock"] == bm.SYNCHRONIZED_WALL
+    assert 0 < t["prepared_execution"]["p20_ms"] <= t["prepared_execution"]["median_ms"] <= t["prepared_execution"]["p80_ms"]
+    assert rec["quality"]["sqnr_db"] > 25 and rec["quality"]["cosine_similarity"] > 0.999
+    assert rec["environment"]["gpu_architecture"] == "sm_100" and rec["extra"]["effective_tflops"] > 0
