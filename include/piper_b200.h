@@ -75,6 +75,14 @@ typedef struct piper_b200_workspace_layout_s {
   int64_t split_units_max;
 } piper_b200_workspace_layout_t;
 
+/* Byte offsets of the intermediates of a SageAttention2++ call (see
+ * sage2pp.cuh in the sources for shapes). */
+typedef struct piper_b200_sage2pp_layout_s {
+  uint64_t q8, qscale, k8, v8t, kscale, kmask, vscale, kmean, ksum, vmax, counter;
+  uint64_t total_bytes;
+  int64_t nk_pad, chunks;
+} piper_b200_sage2pp_layout_t;
+
 /* ABI version of this header (major*100 + minor). */
 int piper_b200_abi_version(void);
 
@@ -197,6 +205,41 @@ int piper_b200_attention_fwd_host(const void* query, const void* key, const void
                                   int dtype, int64_t batch, int64_t heads, int64_t query_length,
                                   int64_t key_length, int64_t head_dim, double scale, int is_causal,
                                   void* scratch, size_t scratch_bytes, void* stream);
+
+/* ---- SageAttention2++ (8+8) --------------------------------------------
+ * The sibling operator of the reference's sage_attention_2pp
+ * (src/piper_kernels/attention/sage_attention_2pp/dispatch.py:37-64, Triton
+ * backend triton.py:1135-1155): INT8 Q/K with per_thread scales (K centred
+ * by its sequence mean), FP8 e4m3 V with per-channel scales, FP8 e4m3
+ * probabilities against the running max shifted by log2(448), and an e4m3 x
+ * e4m3 PV product on the tensor cores (tcgen05 kind::f8f6f4, F32 accumulator).
+ * Same argument conventions as piper_b200_attention_fwd. */
+int piper_b200_sage2pp_layout(int64_t batch, int64_t heads, int64_t query_length,
+                              int64_t key_length, int64_t head_dim,
+                              piper_b200_sage2pp_layout_t* layout);
+
+int piper_b200_sage2pp_workspace_bytes(int64_t batch, int64_t heads, int64_t query_length,
+                                       int64_t key_length, int64_t head_dim, size_t* bytes);
+
+int piper_b200_sage2pp_prepass(const void* query, const int64_t query_strides[3],
+                               const void* key, const int64_t key_strides[3], const void* value,
+                               const int64_t value_strides[3], int dtype, int64_t batch,
+                               int64_t heads, int64_t query_length, int64_t key_length,
+                               int64_t head_dim, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+int piper_b200_sage2pp_attention_prepared(void* out, int dtype, int64_t batch, int64_t heads,
+                                          int64_t query_length, int64_t key_length,
+                                          int64_t head_dim, double scale, int is_causal,
+                                          const void* workspace, size_t workspace_bytes,
+                                          void* stream);
+
+int piper_b200_sage2pp_fwd(const void* query, const int64_t query_strides[3], const void* key,
+                           const int64_t key_strides[3], const void* value,
+                           const int64_t value_strides[3], void* out, int dtype, int64_t batch,
+                           int64_t heads, int64_t query_length, int64_t key_length,
+                           int64_t head_dim, double scale, int is_causal, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Scratch capacity of piper_b200_attention_fwd_no_alloc: 16 MiB per GPU. */
 #define PIPER_B200_NO_ALLOC_WORKSPACE_BYTES (16u * 1024u * 1024u)

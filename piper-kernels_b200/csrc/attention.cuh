@@ -146,6 +146,7 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
 // subtraction converts two values.
 constexpr uint32_t kBiasBits = 0x4B400000u;
 constexpr float kBias = 12582912.0f;
+constexpr float kLog2FP8Max = 8.807354922057604f;  // log2(448): SageAttention2++ P codes top out at 448
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: numerator rescaled only past 2^8 growth
 
 // 2^x for a pair of x <= 0 on the FMA pipe, used for a share of the
@@ -249,7 +250,215 @@ __device__ __forceinline__ WorkUnit decode_unit(const AttnParams& p) {
   return w;
 }
 
+// ---------------------------------------------------------------------------
+// SageAttention2++ (8+8) softmax role, the counterpart of the Piper softmax
+// warpgroups below (sage_attention_2pp/reference.py:63-104):
+//   x      = S*qs_row*ks_key*scale*log2(e) (+ -inf on padded keys)
+//   m'     = max(m, max_k x - log2(448))    running max, shifted so that the
+//                                           block's largest probability is 448
+//   p_k    = 2^(x_k - m')  in [0, 448]      P codes: FP8 e4m3 of p_k
+//   l      = l*2^(m-m') + sum_k p_k
+//   O      = O*2^(m-m') + (P8 . V8)         e4m3 x e4m3 -> F32 on the tensor core
+//   out    = O * vscale / max(l, 1e-30)
+// The 64-key partial is accumulated in F32; the reference rounds it to fp16
+// first (the FP16-accumulating MMA it emulates), a difference at the fp16
+// rounding level.  The per-key K scale and the padded-key mask arrive through
+// the producer's two per-key vector slots.
+struct SoftmaxBars {
+  uint32_t kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag;
+};
+
+// Folds the F32 PV partial of block jj: o += PV * w; the accumulator is
+// released as soon as its last columns are in registers (the next chain
+// overwrites it).
+template <int D>
+__device__ __forceinline__ bool fold_pv_f32(float2 (&o)[D / 2], uint32_t full, uint32_t free_bar, int jj,
+                                            uint32_t tm_pv, float w, int lane, uint64_t budget, uint32_t* status,
+                                            uint32_t abort_flag) {
+  if (!mbar_wait_warp(full, jj & 1, budget, status, kStatusTimeoutMma, abort_flag)) return false;
+  tc_fence_after();
+  const float2 w2 = make_float2(w, w);
+#pragma unroll
+  for (int c = 0; c < D / 64; ++c) {
+    uint32_t v0[32], v1[32];
+    tmem_ld32_split(tm_pv + c * 64, v0);
+    tmem_ld32_split(tm_pv + c * 64 + 32, v1);
+    tmem_ld_wait();
+    if (c == D / 64 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(free_bar);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[c * 32 + i] = __ffma2_rn(f2(v0[2 * i], v0[2 * i + 1]), w2, o[c * 32 + i]);
+      o[c * 32 + 16 + i] = __ffma2_rn(f2(v1[2 * i], v1[2 * i + 1]), w2, o[c * 32 + 16 + i]);
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint32_t e4m3x4(float2 a, float2 b) {
+  uint32_t lo, hi;
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(lo) : "f"(a.y), "f"(a.x));
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(hi) : "f"(b.y), "f"(b.x));
+  return __byte_perm(lo, hi, 0x5410);
+}
+
 template <typename T, int D>
+__device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* smem, uint32_t sbase,
+                                                  uint32_t tmem_base, const SoftmaxBars& bars, int nbt, int64_t q0,
+                                                  int64_t bh, uint32_t* status, uint64_t budget) {
+  using S = AttnSmem<D>;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int t = warp / 4;
+  const int r = threadIdx.x % kTileM;
+  const int row = static_cast<int>(q0) + t * kTileM + r;
+  const bool valid_row = row < p.nq;
+  const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
+  const uint32_t tm_s = tmem_base + lane_base + t * 256;
+  const uint32_t tm_pv = tm_s + 128;
+  const float qs = valid_row ? __ldg(p.qscale + bh * p.nq_all + p.q_row0 + row) : 0.0f;
+  const float c_row = qs * p.scale_log2e;
+  const float2 c2 = make_float2(c_row, c_row);
+  const float2 nb2 = make_float2(-kBias, -kBias);
+  float2 o[D / 2];
+#pragma unroll
+  for (int i = 0; i < D / 2; ++i) o[i] = make_float2(0.0f, 0.0f);
+  float m_run = -INFINITY, l_run = 0.0f, pend_w = 0.0f;
+  bool ok = true;
+  for (int j = 0; j < nbt; ++j) {
+    const int s = j % kStages;
+    const int buf = j & 1;
+    if (!(ok = mbar_wait_warp(bars.kv_full + 8 * s, (j / kStages) & 1, budget, status, kStatusTimeoutFull,
+                              bars.abort_flag)))
+      break;
+    if (!(ok = mbar_wait_warp(bars.s_full + 8 * (t * 2 + buf), (j >> 1) & 1, budget, status, kStatusTimeoutMma,
+                              bars.abort_flag)))
+      break;
+    tc_fence_after();
+    float2 x[kKeyBlock / 2];
+    {
+      uint32_t a[32], b[32];
+      tmem_ld32_split(tm_s + buf * kKeyBlock, a);
+      tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
+      tmem_ld_wait();
+      tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
+      const uint32_t vm = sbase + S::kOffVec + s * S::kVecBytes;  // padded-key mask
+      const uint32_t vk = vm + kKeyBlock * 4;                     // per-key K scale
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 ma = lds128(vm + 16 * i), mb = lds128(vm + 16 * (8 + i));
+        const float4 ka = lds128(vk + 16 * i), kb = lds128(vk + 16 * (8 + i));
+        x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i], a[4 * i + 1]), nb2), __fmul2_rn(c2, make_float2(ka.x, ka.y)),
+                              make_float2(ma.x, ma.y));
+        x[2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2], a[4 * i + 3]), nb2),
+                                  __fmul2_rn(c2, make_float2(ka.z, ka.w)), make_float2(ma.z, ma.w));
+        x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i], b[4 * i + 1]), nb2),
+                                   __fmul2_rn(c2, make_float2(kb.x, kb.y)), make_float2(mb.x, mb.y));
+        x[16 + 2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2], b[4 * i + 3]), nb2),
+                                       __fmul2_rn(c2, make_float2(kb.z, kb.w)), make_float2(mb.z, mb.w));
+      }
+    }
+    if (p.causal) {
+      const int lim = static_cast<int>(
+          max(min(static_cast<int64_t>(row) + p.causal_shift - j * kKeyBlock, static_cast<int64_t>(kKeyBlock)),
+              static_cast<int64_t>(-1)));
+      if (lim < kKeyBlock - 1) {
+#pragma unroll
+        for (int i = 0; i < kKeyBlock / 2; ++i) {
+          if (2 * i > lim) x[i].x = -INFINITY;
+          if (2 * i + 1 > lim) x[i].y = -INFINITY;
+        }
+      }
+    }
+    float mx[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mx[q] = fmaxf(x[q].x, x[q].y);
+#pragma unroll
+    for (int i = 4; i < kKeyBlock / 2; i += 4) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) mx[q] = fmax3(mx[q], x[i + q].x, x[i + q].y);
+    }
+    const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars.s_free + 8 * (t * 2 + buf));
+    // Running max, shifted by log2(448) (reference.py:83-86): rescale the
+    // numerator, the denominator and the partial awaiting its fold.
+    const float msh = mb - kLog2FP8Max;
+    const bool need = msh > m_run;
+    if (__any_sync(0xffffffffu, need)) {
+      const float m_new = need ? msh : m_run;
+      // Lanes that keep their maximum scale by exactly 1 (also when it is
+      // still -inf, where the difference would be NaN).
+      const float w_old = need ? ex2_approx(m_run - m_new) : 1.0f;
+      const float2 w2 = make_float2(w_old, w_old);
+#pragma unroll
+      for (int i = 0; i < D / 2; ++i) o[i] = __fmul2_rn(o[i], w2);
+      l_run *= w_old;
+      pend_w *= w_old;
+      m_run = m_new;
+    }
+    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+    const float2 mneg = make_float2(-m_use, -m_use);
+    float2 ps[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                    make_float2(0.0f, 0.0f)};
+    uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * kKeyBlock;
+    const int sw = (r >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t words[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int w = 4 * c + q;
+        float2 e0 = __fadd2_rn(x[2 * w], mneg);
+        float2 e1 = __fadd2_rn(x[2 * w + 1], mneg);
+        e0 = make_float2(ex2_approx(e0.x), ex2_approx(e0.y));
+        if (q == 0)
+          e1 = exp2_poly2(e1);
+        else
+          e1 = make_float2(ex2_approx(e1.x), ex2_approx(e1.y));
+        ps[q] = __fadd2_rn(ps[q], __fadd2_rn(e0, e1));
+        words[q] = e4m3x4(e0, e1);
+      }
+      *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
+    }
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars.p_full + 8 * (t * 2 + buf));
+    l_run += ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
+    if (j >= 1 && !(ok = fold_pv_f32<D>(o, bars.pv_full + 8 * t, bars.pv_free + 8 * t, j - 1, tm_pv, pend_w, lane,
+                                        budget, status, bars.abort_flag)))
+      break;
+    pend_w = 1.0f;
+  }
+  if (ok && nbt > 0)
+    ok = fold_pv_f32<D>(o, bars.pv_full + 8 * t, bars.pv_free + 8 * t, nbt - 1, tm_pv, pend_w, lane, budget, status,
+                        bars.abort_flag);
+  if (ok && valid_row && flag_get(bars.abort_flag) == 0) {
+    const float inv = 1.0f / fmaxf(l_run, 1e-30f);
+    const float* vs = p.vmean + bh * D;  // per-channel V scale
+    uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + p.q_row0 + row) * D);
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(vs) + 2 * c);
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(vs) + 2 * c + 1);
+      uint4 pk;
+      pk.x = pack2<T>(o[4 * c].x * s0.x * inv, o[4 * c].y * s0.y * inv);
+      pk.y = pack2<T>(o[4 * c + 1].x * s0.z * inv, o[4 * c + 1].y * s0.w * inv);
+      pk.z = pack2<T>(o[4 * c + 2].x * s1.x * inv, o[4 * c + 2].y * s1.y * inv);
+      pk.w = pack2<T>(o[4 * c + 3].x * s1.z * inv, o[4 * c + 3].y * s1.w * inv);
+      orow[c] = pk;
+    }
+  }
+}
+
+template <typename T, int D, bool kSage = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     piper_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
@@ -433,8 +642,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint64_t descV = descV0 + static_cast<uint64_t>(((jp % kStages) * S::kVBytes) >> 4);
             const uint64_t descP = descP0 + static_cast<uint64_t>(((t * 2 + (jp & 1)) * S::kPBytes) >> 4);
             const uint32_t dcol = tmem_base + t * 256 + 128;
+            if constexpr (kSage) {
+              constexpr uint32_t kIdescPVf8 = umma_idesc_e4m3(kTileM, D);
 #pragma unroll
-            for (int kk = 0; kk < kKeyBlock / 32; ++kk) umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, 1u);
+              for (int kk = 0; kk < kKeyBlock / 32; ++kk)
+                umma_f8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf8, kk > 0 ? 1u : 0u);
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < kKeyBlock / 32; ++kk)
+                umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, 1u);
+            }
             umma_commit(pv_full + 8 * t);
             pv_next[t] = jp + 1;
             progress = true;
@@ -466,6 +683,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, budget, status, kStatusTimeoutMma, 0u);
     }
+  } else if constexpr (kSage) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag};
+    sage_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, status, budget);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     // -------------------------------------------------- softmax warpgroups

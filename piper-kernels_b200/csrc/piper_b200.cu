@@ -18,6 +18,7 @@
 #include "layout.h"
 #include "piper_b200.h"
 #include "prepass.cuh"
+#include "sage2pp.cuh"
 
 namespace {
 
@@ -75,14 +76,17 @@ int ensure_device(int* device_out) {
   // The attention kernels redistribute registers between warpgroups with
   // setmaxnreg, which is only safe at the launch register count the split was
   // computed for.
-  const void* kernels[4] = {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>),
+  const void* kernels[8] = {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>),
                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>),
                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>)};
-  const int smem_bytes[4] = {piper::AttnSmem<64>::kAlloc, piper::AttnSmem<128>::kAlloc, piper::AttnSmem<64>::kAlloc,
-                             piper::AttnSmem<128>::kAlloc};
-  for (int i = 0; i < 4; ++i) {
-    PIPER_CUDA(cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes[i]));
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, true>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, true>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>),
+                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>)};
+  for (int i = 0; i < 8; ++i) {
+    const int smem_bytes = (i % 2 == 0) ? piper::AttnSmem<64>::kAlloc : piper::AttnSmem<128>::kAlloc;
+    PIPER_CUDA(cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
     cudaFuncAttributes attr;
     PIPER_CUDA(cudaFuncGetAttributes(&attr, kernels[i]));
     if (attr.numRegs != piper::kLaunchRegs)
@@ -774,4 +778,173 @@ extern "C" int piper_b200_attention_fwd_host(const void* query, const void* key,
   const int last = static_cast<int>((P.chunks - 1) % kHostSlots);
   PIPER_CUDA(cudaStreamWaitEvent(s, hs->drained[last], 0));
   return PIPER_B200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// SageAttention2++ (8+8): prepass and attention launches.
+namespace {
+
+template <typename T, int D, bool V16>
+void launch_sage_prepass_t(const piper::SagePrepassArgs& a, int64_t bh, cudaStream_t stream) {
+  const dim3 stats_grid(static_cast<unsigned>(a.L.chunks), static_cast<unsigned>(bh));
+  piper::sage_stats_kernel<T, D, V16><<<stats_grid, piper::kPrepassThreads, 0, stream>>>(a);
+  const int64_t tiles = (std::max(a.nq, a.nk) + piper::kKeyBlock - 1) / piper::kKeyBlock;
+  const dim3 q_grid(static_cast<unsigned>(tiles), static_cast<unsigned>(bh));
+  piper::sage_quantize_kernel<T, D, V16><<<q_grid, piper::kPrepassThreads, 0, stream>>>(a);
+}
+
+template <typename T, int D>
+void launch_sage_prepass_d(const piper::SagePrepassArgs& a, int64_t bh, bool v16, cudaStream_t stream) {
+  if (v16)
+    launch_sage_prepass_t<T, D, true>(a, bh, stream);
+  else
+    launch_sage_prepass_t<T, D, false>(a, bh, stream);
+}
+
+}  // namespace
+
+extern "C" int piper_b200_sage2pp_layout(int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                                         int64_t head_dim, piper_b200_sage2pp_layout_t* layout) {
+  if (layout == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "layout is NULL");
+  if (batch <= 0 || heads <= 0 || query_length <= 0 || key_length <= 0 || head_dim <= 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  *layout = piper::make_sage_layout(batch * heads, query_length, key_length, head_dim);
+  return PIPER_B200_OK;
+}
+
+extern "C" int piper_b200_sage2pp_workspace_bytes(int64_t batch, int64_t heads, int64_t query_length,
+                                                  int64_t key_length, int64_t head_dim, size_t* bytes) {
+  piper_b200_sage2pp_layout_t L;
+  const int rc = piper_b200_sage2pp_layout(batch, heads, query_length, key_length, head_dim, &L);
+  if (rc != PIPER_B200_OK) return rc;
+  if (bytes == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  *bytes = static_cast<size_t>(L.total_bytes);
+  return PIPER_B200_OK;
+}
+
+extern "C" int piper_b200_sage2pp_prepass(const void* query, const int64_t query_strides[3], const void* key,
+                                          const int64_t key_strides[3], const void* value,
+                                          const int64_t value_strides[3], int dtype, int64_t batch, int64_t heads,
+                                          int64_t query_length, int64_t key_length, int64_t head_dim,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, 0);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!query || !key || !value || !workspace || !query_strides || !key_strides || !value_strides)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  const piper_b200_sage2pp_layout_t L = piper::make_sage_layout(bh, query_length, key_length, head_dim);
+  if (workspace_bytes < L.total_bytes)
+    return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL,
+                "workspace needs " + std::to_string(L.total_bytes) + " bytes, got " + std::to_string(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  piper::SagePrepassArgs a{};
+  a.q = query;
+  a.k = key;
+  a.v = value;
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = query_strides[i];
+    a.ks[i] = key_strides[i];
+    a.vs[i] = value_strides[i];
+  }
+  a.heads = heads;
+  a.nq = query_length;
+  a.nk = key_length;
+  a.ws = static_cast<uint8_t*>(workspace);
+  a.L = L;
+  const bool v16 = aligned16(query, query_strides) && aligned16(key, key_strides) && aligned16(value, value_strides);
+  PIPER_CUDA(cudaMemsetAsync(a.ws + L.counter, 0, static_cast<size_t>(bh) * 4, s));
+  if (dtype == PIPER_B200_FLOAT16) {
+    if (head_dim == 64)
+      launch_sage_prepass_d<__half, 64>(a, bh, v16, s);
+    else
+      launch_sage_prepass_d<__half, 128>(a, bh, v16, s);
+  } else {
+    if (head_dim == 64)
+      launch_sage_prepass_d<__nv_bfloat16, 64>(a, bh, v16, s);
+    else
+      launch_sage_prepass_d<__nv_bfloat16, 128>(a, bh, v16, s);
+  }
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
+}
+
+extern "C" int piper_b200_sage2pp_attention_prepared(void* out, int dtype, int64_t batch, int64_t heads,
+                                                     int64_t query_length, int64_t key_length, int64_t head_dim,
+                                                     double scale, int is_causal, const void* workspace,
+                                                     size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  if (!out || !workspace) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  if (!(std::isfinite(scale) && scale > 0.0))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "scale must be finite and positive");
+  if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "output must be 16-byte aligned");
+  int device = 0;
+  if ((rc = ensure_device(&device)) != PIPER_B200_OK) return rc;
+  const int64_t bh = batch * heads;
+  const piper_b200_sage2pp_layout_t L = piper::make_sage_layout(bh, query_length, key_length, head_dim);
+  if (workspace_bytes < L.total_bytes) return fail(PIPER_B200_ERR_WORKSPACE_TOO_SMALL, "workspace too small");
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  const uint64_t d = static_cast<uint64_t>(head_dim);
+  CUtensorMap tmQ, tmK, tmV;
+  if ((rc = encode_map(&tmQ, ws + L.q8, d, query_length, bh, d, query_length * d, static_cast<uint32_t>(d),
+                       piper::kTileM)) != PIPER_B200_OK)
+    return rc;
+  if ((rc = encode_map(&tmK, ws + L.k8, d, key_length, bh, d, key_length * d, static_cast<uint32_t>(d),
+                       piper::kKeyBlock)) != PIPER_B200_OK)
+    return rc;
+  if ((rc = encode_map(&tmV, ws + L.v8t, L.nk_pad, d, bh, L.nk_pad, L.nk_pad * d, piper::kKeyBlock,
+                       static_cast<uint32_t>(d))) != PIPER_B200_OK)
+    return rc;
+  piper::AttnParams p{};
+  p.qscale = reinterpret_cast<const float*>(ws + L.qscale);  // per query row
+  p.vlog2 = reinterpret_cast<const float*>(ws + L.kmask);    // per-key vector slot 0: padded-key mask
+  p.vrcp = reinterpret_cast<const float*>(ws + L.kscale);    // per-key vector slot 1: K scale
+  p.vmean = reinterpret_cast<const float*>(ws + L.vscale);   // per-channel V scale
+  p.out = out;
+  p.heads = heads;
+  p.nq = query_length;
+  p.nk = key_length;
+  p.nk_pad = L.nk_pad;
+  p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
+  p.causal = is_causal ? 1 : 0;
+  p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
+  p.wait_budget_ns = piper::kWaitBudgetNs;
+  p.nq_all = query_length;
+  p.main_units = static_cast<int64_t>(p.q_tiles) * bh;
+  const int64_t units = p.main_units;
+  const dim3 grid = units < (int64_t(1) << 31) ? dim3(static_cast<unsigned>(units), 1)
+                                                : dim3(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PIPER_B200_FLOAT16) {
+    if (head_dim == 64)
+      piper::piper_attention_kernel<__half, 64, true><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+    else
+      piper::piper_attention_kernel<__half, 128, true><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+  } else {
+    if (head_dim == 64)
+      piper::piper_attention_kernel<__nv_bfloat16, 64, true><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+    else
+      piper::piper_attention_kernel<__nv_bfloat16, 128, true><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+  }
+  PIPER_CUDA(cudaGetLastError());
+  return PIPER_B200_OK;
+}
+
+extern "C" int piper_b200_sage2pp_fwd(const void* query, const int64_t query_strides[3], const void* key,
+                                      const int64_t key_strides[3], const void* value, const int64_t value_strides[3],
+                                      void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                                      int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  rc = piper_b200_sage2pp_prepass(query, query_strides, key, key_strides, value, value_strides, dtype, batch, heads,
+                                  query_length, key_length, head_dim, workspace, workspace_bytes, stream);
+  if (rc != PIPER_B200_OK) return rc;
+  return piper_b200_sage2pp_attention_prepared(out, dtype, batch, heads, query_length, key_length, head_dim, scale,
+                                               is_causal, workspace, workspace_bytes, stream);
 }

@@ -49,6 +49,11 @@ EXPORTED_SYMBOLS = (
     "piper_b200_state_bytes",
     "piper_b200_host_scratch_bytes",
     "piper_b200_attention_fwd_host",
+    "piper_b200_sage2pp_layout",
+    "piper_b200_sage2pp_workspace_bytes",
+    "piper_b200_sage2pp_prepass",
+    "piper_b200_sage2pp_attention_prepared",
+    "piper_b200_sage2pp_fwd",
     "piper_b200_device_status",
     "piper_b200_selftest_wait_timeout",
     "piper_b200_selftest_gemm_i8",
@@ -71,6 +76,18 @@ class WorkspaceLayout(ctypes.Structure):
     ] + [(name, ctypes.c_int64) for name in ("q_groups", "k_groups", "nk_pad", "chunks")] + [
         (name, ctypes.c_uint64) for name in ("kv_pack", "kv_pack_bytes", "totals", "split_state")
     ] + [("split_units_max", ctypes.c_int64)]
+
+
+class Sage2ppLayout(ctypes.Structure):
+    """Mirror of ``piper_b200_sage2pp_layout_t``."""
+
+    _fields_ = [
+        (name, ctypes.c_uint64)
+        for name in (
+            "q8", "qscale", "k8", "v8t", "kscale", "kmask", "vscale", "kmean", "ksum", "vmax", "counter",
+            "total_bytes",
+        )
+    ] + [(name, ctypes.c_int64) for name in ("nk_pad", "chunks")]
 
 
 _lock = threading.Lock()
@@ -130,6 +147,20 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
     ]
     lib.piper_b200_attention_fwd_host.restype = ctypes.c_int
+    lib.piper_b200_sage2pp_layout.argtypes = [_I64] * 5 + [ctypes.POINTER(Sage2ppLayout)]
+    lib.piper_b200_sage2pp_layout.restype = ctypes.c_int
+    lib.piper_b200_sage2pp_workspace_bytes.argtypes = [_I64] * 5 + [ctypes.POINTER(ctypes.c_size_t)]
+    lib.piper_b200_sage2pp_workspace_bytes.restype = ctypes.c_int
+    lib.piper_b200_sage2pp_prepass.argtypes = tensor3 + [ctypes.c_int] + [_I64] * 5 + [_VP, ctypes.c_size_t, _VP]
+    lib.piper_b200_sage2pp_prepass.restype = ctypes.c_int
+    lib.piper_b200_sage2pp_attention_prepared.argtypes = [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_sage2pp_attention_prepared.restype = ctypes.c_int
+    lib.piper_b200_sage2pp_fwd.argtypes = tensor3 + [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
+    ]
+    lib.piper_b200_sage2pp_fwd.restype = ctypes.c_int
     lib.piper_b200_device_status.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]
     lib.piper_b200_device_status.restype = ctypes.c_int
     lib.piper_b200_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int), _VP]
@@ -180,6 +211,12 @@ def strides3(tensor) -> _STRIDES:
 def workspace_layout(batch: int, heads: int, nq: int, nk: int, d: int) -> WorkspaceLayout:
     layout = WorkspaceLayout()
     check(library().piper_b200_workspace_layout(batch, heads, nq, nk, d, ctypes.byref(layout)), "workspace layout")
+    return layout
+
+
+def sage2pp_layout(batch: int, heads: int, nq: int, nk: int, d: int) -> Sage2ppLayout:
+    layout = Sage2ppLayout()
+    check(library().piper_b200_sage2pp_layout(batch, heads, nq, nk, d, ctypes.byref(layout)), "sage2pp layout")
     return layout
 
 

@@ -46,3 +46,8 @@ class AcceleratorTarget:
     def supports_tcgen05_int8(self) -> bool:
         """True for sm_100 (B200-class): tcgen05.mma kind::i8 with TMEM accumulators."""
         return self.cuda_capability == (10, 0)
+
+    @property
+    def supports_tcgen05_fp8(self) -> bool:
+        """True for sm_100 (B200-class): tcgen05.mma kind::f8f6f4 (FP8 e4m3) with TMEM accumulators."""
+        return self.cuda_capability == (10, 0)

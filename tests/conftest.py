@@ -22,7 +22,24 @@ def pytest_configure(config: pytest.Config) -> None:
 
 
 def golden_cases() -> list[str]:
-    return sorted(p.stem for p in GOLDEN_DIR.glob("*.npz"))
+    """Piper Attention fixtures (tests/golden/make_golden.py)."""
+    return sorted(p.stem for p in GOLDEN_DIR.glob("*.npz") if not p.stem.startswith("s2pp_"))
+
+
+def sage_cases() -> list[str]:
+    """SageAttention2++ fixtures (tests/golden/make_golden_sage2pp.py)."""
+    return sorted(p.stem for p in GOLDEN_DIR.glob("s2pp_*.npz"))
+
+
+def load_sage_golden(name: str) -> dict:
+    """SageAttention2++ case: inputs in their dtype, everything else as torch tensors."""
+    z = np.load(GOLDEN_DIR / f"{name}.npz")
+    dtype = torch.float16 if str(z["dtype"]) == "float16" else torch.bfloat16
+    case = {k: torch.from_numpy(np.array(z[k])) for k in z.files if k not in ("dtype",)}
+    for key in ("query", "key", "value"):
+        case[key] = torch.from_numpy(z[key].copy()).view(dtype)
+    case.update(dtype=dtype, scale=float(z["scale"]), is_causal=bool(z["is_causal"]))
+    return case
 
 
 def load_golden(name: str) -> dict:

@@ -1,0 +1,192 @@
+"""SageAttention2++ on the GPU vs the oracle and the reference (B200 only).
+
+Prepass codes and scales are integer/byte work and must be bit-exact: the
+oracle runs on the GPU's own K mean (an exact fp64 sum rounded once to fp32,
+which the oracle reproduces), and the FP8 V bytes pin the byte order of the
+packed e4m3 conversion.  Outputs follow the reference's own tolerances
+(tests/attention/sage_attention_2pp/test_triton.py:103-129: mean |err| <
+0.003, max < 0.12 against the quantized reference; mean < 0.01, max < 0.2
+against SDPA for rectangular and strided inputs).  The reference rounds each
+64-key P.V partial to fp16 while this kernel keeps it in FP32, which is why
+the comparison is not bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import load_sage_golden, require_b200, sage_cases
+
+from oracle import oracle, sage2pp
+from piper_kernels import _native, sage_attention_2pp
+from piper_kernels.attention.sage_attention_2pp.b200 import (
+    launch_sage_attention_2pp,
+    prepare_sage_attention_2pp,
+)
+
+pytestmark = pytest.mark.gpu
+
+
+def _cosine(a: torch.Tensor, b: torch.Tensor) -> float:
+    a = a.double().flatten()
+    b = b.double().flatten()
+    return float((a @ b) / (a.norm() * b.norm()))
+
+
+def _check_prepass(q, k, v, is_causal=False):
+    dev = require_b200()
+    prepared = prepare_sage_attention_2pp(q.to(dev), k.to(dev), v.to(dev), is_causal)
+    torch.cuda.synchronize()
+    assert _native.device_status(0) == 0
+    km = prepared.key_mean.cpu().numpy()
+    assert np.array_equal(km, oracle.sequence_mean(oracle._as_f32(k)))
+    ref = sage2pp.prepare(q, k, v, key_mean=km)
+    assert torch.equal(prepared.query_int8.cpu(), ref["query_int8"])
+    assert torch.equal(prepared.query_scale.cpu(), ref["query_scale"])
+    assert torch.equal(prepared.key_int8.cpu(), ref["key_int8"])
+    assert torch.equal(prepared.key_scale.cpu(), ref["key_scale"])
+    assert torch.equal(prepared.value_scale.cpu(), ref["value_scale"])
+    assert torch.equal(prepared.value_fp8.cpu().view(torch.uint8), ref["value_fp8"])
+    nk = k.shape[2]
+    assert not prepared.value_fp8_transposed.view(torch.uint8)[..., nk:].any(), "padded keys must hold zero codes"
+    return prepared, ref
+
+
+def _check_output(actual: torch.Tensor, expected: torch.Tensor, mean_tol=0.003, max_tol=0.12,
+                  cos_min=0.9995) -> None:
+    # cos_min: against the quantized oracle the gap is fp16 rounding of the
+    # partials; against SDPA it is the quantization error itself.
+    assert torch.isfinite(actual).all()
+    err = (actual.float().cpu() - expected.float().cpu()).abs()
+    assert err.mean().item() < mean_tol, err.mean().item()
+    assert err.max().item() < max_tol, err.max().item()
+    assert _cosine(actual.cpu(), expected.cpu()) > cos_min
+
+
+@pytest.mark.parametrize("name", sage_cases())
+def test_prepass_matches_oracle_on_golden_inputs(name: str) -> None:
+    case = load_sage_golden(name)
+    _check_prepass(case["query"], case["key"], case["value"])
+
+
+@pytest.mark.parametrize("name", sage_cases())
+def test_prepass_codes_match_reference_fixtures(name: str) -> None:
+    # The reference's K mean is torch's fp32 mean; the exact mean differs in
+    # the last bit now and then, which moves a K code by one at most rarely.
+    dev = require_b200()
+    case = load_sage_golden(name)
+    prepared = prepare_sage_attention_2pp(case["query"].to(dev), case["key"].to(dev), case["value"].to(dev),
+                                          case["is_causal"])
+    assert torch.equal(prepared.query_int8.cpu(), case["query_int8"])
+    assert torch.equal(prepared.query_scale.cpu(), case["query_scale"])
+    assert torch.equal(prepared.value_fp8.cpu().view(torch.uint8), case["value_fp8"])
+    assert torch.equal(prepared.value_scale.cpu(), case["value_scale"])
+    diff = (prepared.key_int8.cpu().short() - case["key_int8"].short()).abs()
+    assert diff.max().item() <= 1 and (diff > 0).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("name", sage_cases())
+def test_output_matches_reference_fixtures(name: str) -> None:
+    dev = require_b200()
+    case = load_sage_golden(name)
+    with torch.no_grad():
+        out = sage_attention_2pp(case["query"].to(dev), case["key"].to(dev), case["value"].to(dev),
+                                 scale=case["scale"], is_causal=case["is_causal"])
+    torch.cuda.synchronize()
+    assert out.dtype is case["dtype"] and out.shape == case["query"].shape
+    _check_output(out, case["out"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_matches_quantized_oracle(dtype, head_dim, is_causal) -> None:
+    # Shapes of the reference's test_triton_matches_quantized_reference.
+    torch.manual_seed(43)
+    q = torch.randn(1, 2, 193, head_dim, dtype=dtype)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    prepared, ref = _check_prepass(q, k, v, is_causal)
+    actual = launch_sage_attention_2pp(prepared, head_dim ** -0.5)
+    torch.cuda.synchronize()
+    assert _native.device_status(0) == 0
+    expected = sage2pp.attention_prepared(ref, head_dim ** -0.5, is_causal)
+    _check_output(actual, expected)
+
+
+@pytest.mark.parametrize("n", [1, 17, 63, 64, 65, 127, 129, 320, 1000])
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_ragged_lengths_match_oracle(n: int, is_causal: bool) -> None:
+    torch.manual_seed(1000 + n)
+    q = torch.randn(2, 3, n, 64, dtype=torch.bfloat16)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    prepared, ref = _check_prepass(q, k, v, is_causal)
+    actual = launch_sage_attention_2pp(prepared, 0.125)
+    torch.cuda.synchronize()
+    _check_output(actual, sage2pp.attention_prepared(ref, 0.125, is_causal))
+
+
+def test_ragged_offset_key_matches_oracle() -> None:
+    # The reference's test_triton_ragged_offset_key_matches_quantized_reference:
+    # a large common offset on K is removed by the K smoothing.
+    torch.manual_seed(431)
+    q = torch.randn(1, 1, 32, 64, dtype=torch.float16)
+    k = 100.0 + torch.randn(1, 1, 17, 64, dtype=torch.float16)
+    v = torch.randn_like(k)
+    prepared, ref = _check_prepass(q, k, v)
+    actual = launch_sage_attention_2pp(prepared, 64 ** -0.5)
+    torch.cuda.synchronize()
+    _check_output(actual, sage2pp.attention_prepared(ref, 64 ** -0.5, False))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_rectangular_and_strided_inputs(dtype, head_dim) -> None:
+    dev = require_b200()
+    torch.manual_seed(44)
+    qs = torch.randn(2, 2, 194, head_dim, device=dev, dtype=dtype)
+    ks = torch.randn(2, 2, 286, head_dim, device=dev, dtype=dtype)
+    vs = torch.randn_like(ks)
+    q, k, v = qs[:, :, ::2], ks[:, :, ::2], vs[:, :, ::2]
+    with torch.no_grad():
+        actual = sage_attention_2pp(q, k, v)
+        expected = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    torch.cuda.synchronize()
+    assert actual.shape == q.shape
+    _check_output(actual, expected, mean_tol=0.01, max_tol=0.2, cos_min=0.999)
+    _, ref = _check_prepass(q.cpu(), k.cpu(), v.cpu())
+    _check_output(actual, sage2pp.attention_prepared(ref, head_dim ** -0.5, False))
+
+
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_long_sequence_against_sdpa(is_causal: bool) -> None:
+    # The reference's long causal schedule case (test_triton.py:318-340),
+    # checked against SDPA by cosine since the oracle would be slow here.
+    dev = require_b200()
+    torch.manual_seed(442)
+    q = torch.randn(1, 8, 4224, 128, device=dev, dtype=torch.bfloat16)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    with torch.no_grad():
+        actual = sage_attention_2pp(q, k, v, is_causal=is_causal)
+        expected = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=is_causal)
+    torch.cuda.synchronize()
+    assert _native.device_status(0) == 0
+    assert torch.isfinite(actual).all()
+    assert _cosine(actual, expected) > 0.999
+    assert (actual.float() - expected.float()).abs().mean().item() < 0.01
+
+
+def test_runs_under_torch_compile() -> None:
+    dev = require_b200()
+    torch.manual_seed(45)
+    q = torch.randn(1, 2, 130, 64, device=dev, dtype=torch.float16)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    compiled = torch.compile(lambda a, b, c: sage_attention_2pp(a, b, c), fullgraph=True)
+    with torch.no_grad():
+        eager = sage_attention_2pp(q, k, v)
+        traced = compiled(q, k, v)
+    assert torch.equal(eager, traced)
