@@ -9,24 +9,25 @@ versioned record per provider and shape:
      "shape": {...}, "configuration": {...}, "timings": {...},
      "quality": {...}, "environment": {...}, "extra": {...}}
 
-This module produces the same fields for the sm_100a operator, so records of
-both implementations can be compared key by key.  The standard phases are:
+This module produces the same fields for the sm_100a operators
+(``piper_attention`` and ``sage_attention_2pp``), so records of both
+implementations can be compared key by key.  The standard phases are:
 
-* ``first_call_ms``: the synchronized first ``piper_attention`` call;
+* ``first_call_ms``: the synchronized first call of the operator;
 * ``preparation``: the quantization prepass (synchronized wall clock);
 * ``prepared_execution``: the fused attention kernel on prepared operands
   (CUDA events on the launching stream);
-* ``operator_end_to_end``: the whole ``piper_attention`` call (synchronized
-  wall clock).
+* ``operator_end_to_end``: the whole operator call (synchronized wall
+  clock).
 
 Each timing is a median with its 20th and 80th percentiles over repeated
 runs filling ``measurement_time_ms``.  Quality compares the output with a
 float32 reference (PyTorch SDPA by default) in float64 arithmetic.
 
-Command line (one JSON Lines record per sequence length):
+Command line (one JSON Lines record per operator and sequence length):
 
     python -m piper_kernels.benchmarking --heads 24 --sequence 4096 16384 \\
-        --output records.jsonl
+        --operator piper_attention sage_attention_2pp --output records.jsonl
 """
 
 from __future__ import annotations
@@ -49,6 +50,7 @@ import torch
 
 SCHEMA_VERSION = 1
 PROVIDER = "piper_b200"
+SAGE_PROVIDER = "sage_attention_2pp_b200"
 DEVICE_EVENT = "device_event"
 SYNCHRONIZED_WALL = "synchronized_wall"
 
@@ -344,6 +346,51 @@ def sdpa_reference(query, key, value, scale: float, is_causal: bool) -> torch.Te
         query.float(), key.float(), value.float(), is_causal=is_causal, scale=scale)
 
 
+def _measure(query, key, value, *, operator: str, provider: str, is_causal: bool, scale: float | None,
+             seed: int | None, warmup_ms: int, measurement_time_ms: int, reference: torch.Tensor | None,
+             public: Callable, prepare: Callable, launch: Callable, saturation_of: Callable,
+             configuration: Mapping[str, Any]) -> BenchmarkRecord:
+    scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
+    stream = torch.cuda.current_stream(query.device)
+    sync = torch.cuda.synchronize
+    with torch.no_grad():
+        sync()
+        t = time.perf_counter()
+        out = public(query, key, value, scale=scale, is_causal=is_causal)
+        sync()
+        first_ms = (time.perf_counter() - t) * 1e3
+        prep = Timing.from_samples(_wall_samples(lambda: prepare(query, key, value, is_causal),
+                                                 warmup_ms, measurement_time_ms, sync), SYNCHRONIZED_WALL)
+        prepared = prepare(query, key, value, is_causal)
+        buf = torch.empty_like(query, memory_format=torch.contiguous_format)
+        run = Timing.from_samples(_event_samples(lambda: launch(prepared, scale, out=buf),
+                                                 warmup_ms, measurement_time_ms, stream), DEVICE_EVENT)
+        e2e = Timing.from_samples(_wall_samples(lambda: public(query, key, value, scale=scale, is_causal=is_causal),
+                                                warmup_ms, measurement_time_ms, sync), SYNCHRONIZED_WALL)
+        expected = sdpa_reference(query, key, value, scale, is_causal) if reference is None else reference
+        quality = measure_quality(out, expected.to(out.device), saturation_of(prepared, key.shape[2]))
+    shape = attention_shape(query, key)
+    config = {
+        "dtype": str(query.dtype).replace("torch.", ""),
+        "is_causal": is_causal,
+        "scale": scale,
+        "seed": seed,
+        "implementation": "sm100a_cuda",
+        "algorithm": operator,
+        **configuration,
+    }
+    return BenchmarkRecord(
+        benchmark="attention",
+        provider=provider,
+        shape=shape,
+        configuration=config,
+        timings=PhaseTimings(warmup_ms, measurement_time_ms, first_ms, prep, run, e2e),
+        environment=capture_environment(device=query.device),
+        quality=quality,
+        extra={"effective_tflops": effective_tflops(shape, is_causal, run.median_ms)},
+    )
+
+
 def measure_piper_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, *,
                             is_causal: bool = False, scale: float | None = None, seed: int | None = None,
                             warmup_ms: int = 100, measurement_time_ms: int = 500,
@@ -352,58 +399,51 @@ def measure_piper_attention(query: torch.Tensor, key: torch.Tensor, value: torch
     from . import piper_attention
     from .attention.piper_attention.b200 import launch_piper_attention, prepare_piper_attention
 
-    scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
-    stream = torch.cuda.current_stream(query.device)
-    sync = torch.cuda.synchronize
-    with torch.no_grad():
-        sync()
-        t = time.perf_counter()
-        out = piper_attention(query, key, value, scale=scale, is_causal=is_causal)
-        sync()
-        first_ms = (time.perf_counter() - t) * 1e3
-        prep = Timing.from_samples(_wall_samples(lambda: prepare_piper_attention(query, key, value, is_causal),
-                                                 warmup_ms, measurement_time_ms, sync), SYNCHRONIZED_WALL)
-        prepared = prepare_piper_attention(query, key, value, is_causal)
-        buf = torch.empty_like(query, memory_format=torch.contiguous_format)
-        run = Timing.from_samples(_event_samples(lambda: launch_piper_attention(prepared, scale, out=buf),
-                                                 warmup_ms, measurement_time_ms, stream), DEVICE_EVENT)
-        e2e = Timing.from_samples(_wall_samples(lambda: piper_attention(query, key, value, scale=scale,
-                                                                        is_causal=is_causal),
-                                                warmup_ms, measurement_time_ms, sync), SYNCHRONIZED_WALL)
-        expected = sdpa_reference(query, key, value, scale, is_causal) if reference is None else reference
-        saturation = {
+    def saturation_of(prepared, nk: int) -> dict[str, Saturation]:
+        return {
             "query_int8": measure_saturation(prepared.query_int8, -127, 127),
             "key_int8": measure_saturation(prepared.key_int8, -127, 127),
-            "value_int8": measure_saturation(prepared.value_int8_transposed[..., : key.shape[2]], -127, 127),
+            "value_int8": measure_saturation(prepared.value_int8_transposed[..., :nk], -127, 127),
         }
-        quality = measure_quality(out, expected.to(out.device), saturation)
-    shape = attention_shape(query, key)
-    configuration = {
-        "dtype": str(query.dtype).replace("torch.", ""),
-        "is_causal": is_causal,
-        "scale": scale,
-        "seed": seed,
-        "implementation": "sm100a_cuda",
-        "algorithm": "piper_attention",
-        "qk_quantization": "per_warp",
-        "probability_dtype": "uint8",
-        "value_dtype": "int8",
-        "value_scale": "per_key",
-    }
-    return BenchmarkRecord(
-        benchmark="attention",
-        provider=PROVIDER,
-        shape=shape,
-        configuration=configuration,
-        timings=PhaseTimings(warmup_ms, measurement_time_ms, first_ms, prep, run, e2e),
-        environment=capture_environment(device=query.device),
-        quality=quality,
-        extra={"effective_tflops": effective_tflops(shape, is_causal, run.median_ms)},
-    )
+
+    return _measure(query, key, value, operator="piper_attention", provider=PROVIDER, is_causal=is_causal,
+                    scale=scale, seed=seed, warmup_ms=warmup_ms, measurement_time_ms=measurement_time_ms,
+                    reference=reference, public=piper_attention, prepare=prepare_piper_attention,
+                    launch=launch_piper_attention, saturation_of=saturation_of,
+                    configuration={"qk_quantization": "per_warp", "probability_dtype": "uint8",
+                                   "value_dtype": "int8", "value_scale": "per_key"})
+
+
+def measure_sage_attention_2pp(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, *,
+                               is_causal: bool = False, scale: float | None = None, seed: int | None = None,
+                               warmup_ms: int = 100, measurement_time_ms: int = 500,
+                               reference: torch.Tensor | None = None) -> BenchmarkRecord:
+    """One record for ``sage_attention_2pp`` (configuration keys of the reference's Sage provider)."""
+    from . import sage_attention_2pp
+    from .attention.sage_attention_2pp.b200 import launch_sage_attention_2pp, prepare_sage_attention_2pp
+
+    def saturation_of(prepared, _nk: int) -> dict[str, Saturation]:
+        return {
+            "query_int8": measure_saturation(prepared.query_int8, -127, 127),
+            "key_int8": measure_saturation(prepared.key_int8, -127, 127),
+        }
+
+    return _measure(query, key, value, operator="sage_attention_2pp", provider=SAGE_PROVIDER,
+                    is_causal=is_causal, scale=scale, seed=seed, warmup_ms=warmup_ms,
+                    measurement_time_ms=measurement_time_ms, reference=reference, public=sage_attention_2pp,
+                    prepare=prepare_sage_attention_2pp, launch=launch_sage_attention_2pp,
+                    saturation_of=saturation_of,
+                    configuration={"qk_quantization": "per_thread", "probability_dtype": "float8_e4m3fn",
+                                   "value_dtype": "float8_e4m3fn", "value_scale": "per_channel",
+                                   "pv_accumulation": "fp32", "block_n": 64})
+
+
+MEASURES = {"piper_attention": measure_piper_attention, "sage_attention_2pp": measure_sage_attention_2pp}
 
 
 def main(argv: list[str] | None = None) -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--operator", choices=sorted(MEASURES), nargs="+", default=["piper_attention"])
     parser.add_argument("--batch-size", type=int, default=1)
     parser.add_argument("--heads", type=int, default=24)
     parser.add_argument("--sequence", type=int, nargs="+", default=[4096])
@@ -427,13 +467,14 @@ def main(argv: list[str] | None = None) -> None:
         q = torch.randn((args.batch_size, args.heads, n, args.head_dim), generator=g, device=dev).to(dtype)
         k = torch.randn((args.batch_size, args.heads, nk, args.head_dim), generator=g, device=dev).to(dtype)
         v = torch.randn((args.batch_size, args.heads, nk, args.head_dim), generator=g, device=dev).to(dtype)
-        rec = measure_piper_attention(q, k, v, is_causal=args.causal, scale=args.scale, seed=args.seed,
-                                      warmup_ms=args.warmup_ms, measurement_time_ms=args.measurement_time_ms)
-        records.append(rec)
-        t = rec.timings
-        print(f"{PROVIDER} N={n}: prepared {t.prepared_execution.median_ms:.3f} ms "
-              f"({rec.extra['effective_tflops']:.1f} TFLOPS-equivalent), end-to-end "
-              f"{t.operator_end_to_end.median_ms:.3f} ms, SQNR {rec.quality.sqnr_db:.1f} dB", flush=True)
+        for operator in args.operator:
+            rec = MEASURES[operator](q, k, v, is_causal=args.causal, scale=args.scale, seed=args.seed,
+                                     warmup_ms=args.warmup_ms, measurement_time_ms=args.measurement_time_ms)
+            records.append(rec)
+            t = rec.timings
+            print(f"{rec.provider} N={n}: prepared {t.prepared_execution.median_ms:.3f} ms "
+                  f"({rec.extra['effective_tflops']:.1f} TFLOPS-equivalent), end-to-end "
+                  f"{t.operator_end_to_end.median_ms:.3f} ms, SQNR {rec.quality.sqnr_db:.1f} dB", flush=True)
     if args.output is not None:
         write_records(records, args.output, args.format)
 

@@ -190,3 +190,18 @@ def test_runs_under_torch_compile() -> None:
         eager = sage_attention_2pp(q, k, v)
         traced = compiled(q, k, v)
     assert torch.equal(eager, traced)
+
+
+def test_benchmark_record_through_the_gpu() -> None:
+    from piper_kernels import benchmarking as bm
+
+    dev = require_b200()
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn((1, 4, 1024, 128), generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    rec = bm.measure_sage_attention_2pp(q, k, v, warmup_ms=5, measurement_time_ms=20).as_dict()
+    assert rec["provider"] == bm.SAGE_PROVIDER
+    assert rec["configuration"]["algorithm"] == "sage_attention_2pp"
+    assert rec["configuration"]["qk_quantization"] == "per_thread"
+    t = rec["timings"]
+    assert 0 < t["prepared_execution"]["p20_ms"] <= t["prepared_execution"]["median_ms"] <= t["prepared_execution"]["p80_ms"]
+    assert rec["quality"]["sqnr_db"] > 25 and rec["quality"]["cosine_similarity"] > 0.999
