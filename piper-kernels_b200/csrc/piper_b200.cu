@@ -93,6 +93,10 @@ int ensure_device(int* device_out) {
       return fail(PIPER_B200_ERR_CUDA, "attention kernel compiled with " + std::to_string(attr.numRegs) +
                                            " registers per thread; its warpgroup register split needs " +
                                            std::to_string(piper::kLaunchRegs));
+    int resident = 0;
+    PIPER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kernels[i], piper::kAttnThreads, smem_bytes));
+    if (resident < 1)
+      return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE, "an attention CTA does not fit on one SM of this device");
   }
   g_device_ready[device] = true;
   return PIPER_B200_OK;
