@@ -10,22 +10,31 @@
 //     e_k    = 2^(x_k - mb)  (= p_k * vs_k, in [0,1])
 //     P8_k   = round_half_even(255 * e_k)                  (UINT8 codes)
 //     l      = l*2^(m-m') + (sum_k e_k / vs_k) * 2^(mb-m')  (FP32 denominator on unquantized p)
-//     O      = O*2^(m-m') + (P8 . V8) * 2^(mb-m')/255      (UINT8 x INT8 -> INT32, tensor cores)
+//     O      = O*2^(m-m') + (P8 . V8) * 2^(mb-m')/255      (the numerator)
 //   out = O / max(l, 1e-30) + mean_V
 // which is the reference's arithmetic with exp/log taken base 2 (identical
 // maxima and weights; rounding differs at the last-ulp level only).
 //
+// The numerator is accumulated by the tensor cores in F32 in TMEM across all
+// blocks: each UINT8 code is written as the fp16 value P8_k * 2^(mb-m')/255
+// (times a constant; one fp16 rounding), V codes are fp16 (exact), and the
+// PV product is one tcgen05 kind::f16 MMA per 16 keys.  The codes are the
+// reference's; only the per-block weight is applied per code instead of per
+// INT32 block sum.  The lazy rescale (m' moves by more than 2^8) scales O in
+// TMEM.
+//
 // CTA = 384 threads, one CTA per SM (TMEM: all 512 columns):
-//   warpgroup 0 / 1  softmax + numerator for Q tile 0 / 1 (128 rows each;
-//                    thread i owns row i = TMEM lane i; fp32 O in registers)
+//   warpgroup 0 / 1  softmax for Q tile 0 / 1 (128 rows each; thread i owns
+//                    row i = TMEM lane i)
 //   warp 8           TMA producer: Q tiles once, then K, V^T tiles and the
-//                    per-key log2(vs), 1/vs vectors into a kStages ring
+//                    per-key log2(vs), 1/vs vectors into a K/V ring
 //   warp 9           TMEM allocator + single-thread tcgen05.mma issuer,
 //                    event driven: QK^T and PV of each tile issued as soon
-//                    as their operands and accumulators are ready
+//                    as their operands are ready
 // Shared-memory operands are in the canonical 128B/64B-swizzled K-major
-// layouts TMA writes; P codes are written by the softmax threads into the
-// same 64B-swizzled layout.  No multicast anywhere.
+// layouts TMA writes; P is written by the softmax threads into the same
+// 128B-swizzled layout.  No multicast anywhere.  The SageAttention2++ kernel
+// (kSage) shares this skeleton with e4m3 P/V and a per-block F32 partial.
 //
 // Sequence shards (ring attention): the recurrence above is associative over
 // key blocks, so a launch may cover one shard of the keys and carry each
@@ -49,7 +58,6 @@ namespace piper {
 constexpr int kAttnThreads = 384;
 constexpr int kTileM = 128;  // query rows per softmax warpgroup
 constexpr int kTiles = 2;    // Q tiles per CTA
-constexpr int kStages = 6;   // K/V ring depth
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s per wait
 // Register split (setmaxnreg): launch = 168 x 384 = 64512 registers; control
 // warpgroup 40, the two softmax warpgroups 232: 128*40 + 256*232 = 64512.
@@ -63,12 +71,18 @@ static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kLaunchRegs * kAttnThre
 
 __device__ uint32_t g_piper_status = 0;
 
-template <int D>
+// Shared memory of one CTA.  kWide: the PV operands are 16-bit (Piper: fp16
+// V codes and weighted fp16 probabilities, rows of 128 B, SW128); otherwise
+// 8-bit (SageAttention2++: e4m3, rows of 64 B, SW64).
+template <int D, bool kWide = false>
 struct AttnSmem {
+  static constexpr int kStages = (kWide && D == 128) ? 5 : 6;  // K/V ring depth
+  static constexpr int kPVElem = kWide ? 2 : 1;                 // bytes per V / P element
   static constexpr int kQBytes = kTileM * D;       // one Q tile (SW128 for D=128, SW64 for D=64)
   static constexpr int kKBytes = kKeyBlock * D;    // one K block
-  static constexpr int kVBytes = D * kKeyBlock;    // one V^T block (D rows x 64 keys, SW64)
-  static constexpr int kPBytes = kTileM * kKeyBlock;  // one P tile (128 rows x 64 keys, SW64)
+  static constexpr int kVBytes = D * kKeyBlock * kPVElem;    // one V^T block (D rows x 64 keys)
+  static constexpr int kPBytes = kTileM * kKeyBlock * kPVElem;  // one P tile (128 rows x 64 keys)
+  static constexpr int kPVRow = kKeyBlock * kPVElem;  // bytes per V^T / P row: the swizzle width
   static constexpr int kVecBytes = 2 * kKeyBlock * 4;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kTiles * kQBytes;
@@ -81,6 +95,9 @@ struct AttnSmem {
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
 };
+
+static_assert(AttnSmem<128, true>::kAlloc <= 232448 && AttnSmem<128>::kAlloc <= 232448,
+              "attention shared memory exceeds 227 KB");
 
 struct AttnParams {
   const float* qscale;
@@ -193,43 +210,6 @@ __device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
   for (int c = 0; c < kCols; c += 4) tmem_st4_same(taddr + c, kBiasBits);
 }
 
-// Folds the INT32 PV partial of block jj (in TMEM) into the fp32 numerator
-// held in registers (reference.py:113; the reference's numerator *= old_weight
-// of reference.py:102 is applied lazily by the caller).  The accumulator is
-// read as the float bias + PV, and folded as is, o += (bias + PV) * w: one
-// packed FMA per two columns.  The caller repeats the same FMA on the bias
-// alone (bias_acc = fma(bias, w, bias_acc)) and subtracts bias_acc once in the
-// epilogue, so a zero PV cancels exactly (constant V is restored bit for bit);
-// otherwise the cost is fp32 rounding at the magnitude of bias * sum(w),
-// about 1e-4 of the output scale.
-template <int D>
-__device__ __forceinline__ bool fold_pv(float2 (&o)[D / 2], uint32_t full, uint32_t free_bar, int jj,
-                                        uint32_t tm_pv, float w, int lane, uint64_t budget, uint32_t* status,
-                                        uint32_t abort_flag) {
-  if (!mbar_wait_warp(full, jj & 1, budget, status, kStatusTimeoutMma, abort_flag)) return false;
-  tc_fence_after();
-  const float2 w2 = make_float2(w, w);
-#pragma unroll
-  for (int c = 0; c < D / 64; ++c) {
-    uint32_t v0[32], v1[32];
-    tmem_ld32_split(tm_pv + c * 64, v0);
-    tmem_ld32_split(tm_pv + c * 64 + 32, v1);
-    tmem_ld_wait();
-    // Re-arm these columns now; the store completes while the math runs.
-    tmem_fill_bias<64>(tm_pv + c * 64);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[c * 32 + i] = __ffma2_rn(f2(v0[2 * i], v0[2 * i + 1]), w2, o[c * 32 + i]);
-      o[c * 32 + 16 + i] = __ffma2_rn(f2(v1[2 * i], v1[2 * i + 1]), w2, o[c * 32 + 16 + i]);
-    }
-  }
-  tmem_st_wait();
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(free_bar);
-  return true;
-}
-
 // Work unit of this CTA: the tile it takes and, for a CTA of the split tail,
 // its key range (split >= 0).  Cheap enough to recompute where needed, so no
 // register carries it across the main loop.
@@ -331,9 +311,9 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
   float m_run = -INFINITY, l_run = 0.0f, pend_w = 0.0f;
   bool ok = true;
   for (int j = 0; j < nbt; ++j) {
-    const int s = j % kStages;
+    const int s = j % S::kStages;
     const int buf = j & 1;
-    if (!(ok = mbar_wait_warp(bars.kv_full + 8 * s, (j / kStages) & 1, budget, status, kStatusTimeoutFull,
+    if (!(ok = mbar_wait_warp(bars.kv_full + 8 * s, (j / S::kStages) & 1, budget, status, kStatusTimeoutFull,
                               bars.abort_flag)))
       break;
     if (!(ok = mbar_wait_warp(bars.s_full + 8 * (t * 2 + buf), (j >> 1) & 1, budget, status, kStatusTimeoutMma,
@@ -458,12 +438,328 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
   }
 }
 
+// Scale of the fp16 probabilities: the PV operand of block j is
+// code * w_j * kPScale / 255 (w_j = 2^(max_j - m_ref) <= 2^8), so the numerator
+// in TMEM carries a factor kPScale, removed in the epilogue.  32 keeps every
+// operand and the constants below within fp16 range.
+constexpr float kPScale = 32.0f;
+
+// Piper softmax warpgroups (reference.py:61-118): thread i of warpgroup t owns
+// query row i of tile t (TMEM lane i).  Per 64-key block it converts the
+// INT32 scores, takes the block max, applies the lazy rescale, and writes the
+// UINT8 codes round(255 * 2^(x - max)) -- each already multiplied by its
+// block weight, as fp16 -- for an fp16 PV MMA that accumulates the numerator
+// in F32 in TMEM across all blocks.  The weighting is exact up to one fp16
+// rounding per probability: the code bits c from the +1.5*2^23 add are placed
+// under an fp16 exponent (2 + c/512), and one HFMA2 with the power-of-two
+// multiples 512*w and -1024*w of the fp16 weight w gives c*w.
+template <typename T, int D>
+__device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t* smem, uint32_t sbase,
+                                                   uint32_t tmem_base, const SoftmaxBars& bars, int nbt, int64_t q0,
+                                                   int64_t bh, int split, int64_t key0, uint32_t* status,
+                                                   uint64_t budget) {
+  using S = AttnSmem<D, true>;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int t = warp / 4;
+  const int r = threadIdx.x % kTileM;
+  const int row = static_cast<int>(q0) + t * kTileM + r;
+  const bool valid_row = row < p.nq;
+  const int64_t grow = p.q_row0 + row;  // row within the head's nq_all rows
+  const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
+  const uint32_t tm_s = tmem_base + lane_base + t * 256;
+  const uint32_t tm_o = tm_s + 128;
+  const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + grow / kQueryGroup) : 0.0f;
+  const float c_row = qs * p.scale_log2e;
+  const float* kscale = p.kscale + bh * p.k_groups + key0 / kKeyGroup;
+  const float2 nb2 = make_float2(-kBias, -kBias);
+
+  // m_ref: reference max of the numerator and denominator (log2 units).  It
+  // trails the true running max by less than kRescaleThreshold, which leaves
+  // O/l unchanged and skips almost every rescale.
+  float m_ref = -INFINITY, l_run = 0.0f;
+  bool ok = true;
+  int pv_seen = 0;  // pv_full completions consumed (one per block)
+  // In a split tile only key range 0 continues from the carried state; the
+  // merge combines the ranges.
+  const bool load = (p.state_mode & kStateLoad) && split <= 0;
+  if (load) {
+    // Continue the recurrence of earlier key shards: the carried numerator
+    // goes into TMEM (x kPScale) before the first PV MMA accumulates onto it.
+    const float4* so = reinterpret_cast<const float4*>(p.state_o + (bh * p.nq_all + grow) * D);
+#pragma unroll 4
+    for (int c = 0; c < D / 8; ++c) {
+      uint32_t v[8];
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (valid_row) {
+        a = so[2 * c];
+        b = so[2 * c + 1];
+      }
+      v[0] = __float_as_uint(a.x * kPScale);
+      v[1] = __float_as_uint(a.y * kPScale);
+      v[2] = __float_as_uint(a.z * kPScale);
+      v[3] = __float_as_uint(a.w * kPScale);
+      v[4] = __float_as_uint(b.x * kPScale);
+      v[5] = __float_as_uint(b.y * kPScale);
+      v[6] = __float_as_uint(b.z * kPScale);
+      v[7] = __float_as_uint(b.w * kPScale);
+      tmem_st8(tm_o + 8 * c, v);
+    }
+    tmem_st_wait();
+    if (valid_row) {
+      const float2 ml = reinterpret_cast<const float2*>(p.state_ml)[bh * p.nq_all + grow];
+      m_ref = ml.x;
+      l_run = ml.y;
+    }
+  }
+
+  for (int j = 0; j < nbt; ++j) {
+    const int s = j % S::kStages;
+    const int buf = j & 1;
+    const float ks = __ldg(kscale + j);
+    if (!(ok = mbar_wait_warp(bars.kv_full + 8 * s, (j / S::kStages) & 1, budget, status, kStatusTimeoutFull,
+                              bars.abort_flag)))
+      break;
+    if (!(ok = mbar_wait_warp(bars.s_full + 8 * (t * 2 + buf), (j >> 1) & 1, budget, status, kStatusTimeoutMma,
+                              bars.abort_flag)))
+      break;
+    tc_fence_after();
+    float2 x[kKeyBlock / 2];
+    {
+      uint32_t a[32], b[32];
+      tmem_ld32_split(tm_s + buf * kKeyBlock, a);
+      tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
+      tmem_ld_wait();
+      // Re-arm the S buffer; s_free is signalled after the block max, by
+      // which time this store has long completed.
+      tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
+      const float c = c_row * ks;
+      const float2 c2 = make_float2(c, c);
+      const uint32_t vl = sbase + S::kOffVec + s * S::kVecBytes;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 la = lds128(vl + 16 * i), lb = lds128(vl + 16 * (8 + i));
+        x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i], a[4 * i + 1]), nb2), c2, make_float2(la.x, la.y));
+        x[2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2], a[4 * i + 3]), nb2), c2, make_float2(la.z, la.w));
+        x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i], b[4 * i + 1]), nb2), c2, make_float2(lb.x, lb.y));
+        x[16 + 2 * i + 1] =
+            __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2], b[4 * i + 3]), nb2), c2, make_float2(lb.z, lb.w));
+      }
+    }
+    if (p.causal) {
+      // Keys after this row are masked (reference.py:86-91); only the
+      // diagonal block needs work: lim = last visible key - first key of
+      // the block, clamped to [-1, 64].
+      const int lim = static_cast<int>(
+          max(min(static_cast<int64_t>(row) + p.causal_shift - j * kKeyBlock, static_cast<int64_t>(kKeyBlock)),
+              static_cast<int64_t>(-1)));
+      if (lim < kKeyBlock - 1) {
+#pragma unroll
+        for (int i = 0; i < kKeyBlock / 2; ++i) {
+          if (2 * i > lim) x[i].x = -INFINITY;
+          if (2 * i + 1 > lim) x[i].y = -INFINITY;
+        }
+      }
+    }
+    // Block max (reference.py:94-95), four independent 3-input chains.
+    float mx[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mx[q] = fmaxf(x[q].x, x[q].y);
+#pragma unroll
+    for (int i = 4; i < kKeyBlock / 2; i += 4) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) mx[q] = fmax3(mx[q], x[i + q].x, x[i + q].y);
+    }
+    const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars.s_free + 8 * (t * 2 + buf));
+    // Lazy rescale of numerator and denominator (exact identity).  The
+    // numerator lives in TMEM: it is scaled there once the PV MMAs of the
+    // earlier blocks have completed.
+    const bool need = mb > m_ref + kRescaleThreshold;
+    if (__any_sync(0xffffffffu, need)) {
+      const float new_ref = need ? mb : m_ref;
+      const float w_old = need ? ex2_approx(m_ref - new_ref) : 1.0f;
+      if (j >= 1 || load) {
+        if (j >= 1 && pv_seen < j) {
+          if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
+                                    bars.abort_flag)))
+            break;
+          pv_seen = j;
+        }
+        tc_fence_after();
+        const float2 w2 = make_float2(w_old, w_old);
+#pragma unroll 2
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32_split(tm_o + 32 * c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 y = __fmul2_rn(f2(v[2 * i], v[2 * i + 1]), w2);
+            v[2 * i] = __float_as_uint(y.x);
+            v[2 * i + 1] = __float_as_uint(y.y);
+          }
+          tmem_st8(tm_o + 32 * c, v);
+          tmem_st8(tm_o + 32 * c + 8, v + 8);
+          tmem_st8(tm_o + 32 * c + 16, v + 16);
+          tmem_st8(tm_o + 32 * c + 24, v + 24);
+        }
+        tmem_st_wait();
+      }
+      l_run *= w_old;
+      m_ref = new_ref;
+    }
+    // Probabilities relative to the block max: e = p * vs in [0,1]
+    // (reference.py:99, 104-108); UINT8 codes round(255 e) half-to-even,
+    // stored as code * w_j * kPScale / 255 in fp16.
+    const float m_use = (mb == -INFINITY) ? 0.0f : mb;
+    const float2 mneg = make_float2(-m_use, -m_use);
+    const float w_cur = (mb == -INFINITY) ? 0.0f : ex2_approx(mb - m_ref);
+    const __half wh = __float2half_rn(w_cur * (kPScale / 255.0f));
+    const __half2 w512 = __half2half2(__hmul(wh, __float2half_rn(512.0f)));
+    const __half2 w1024n = __half2half2(__hneg(__hmul(wh, __float2half_rn(1024.0f))));
+    const uint32_t vr = sbase + S::kOffVec + s * S::kVecBytes + kKeyBlock * 4;
+    float2 ps[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                    make_float2(0.0f, 0.0f)};
+    const float2 k255 = make_float2(255.0f, 255.0f);
+    const float2 kb2 = make_float2(kBias, kBias);
+    uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * S::kPVRow;
+    const int sw = r & 7;  // 128B swizzle: 16-byte chunk index ^ (row % 8)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {  // 8 keys per 16-byte chunk
+      const float4 ra = lds128(vr + 32 * c), rb = lds128(vr + 32 * c + 16);
+      const float2 rv[4] = {make_float2(ra.x, ra.y), make_float2(ra.z, ra.w), make_float2(rb.x, rb.y),
+                            make_float2(rb.z, rb.w)};
+      uint32_t words[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 e = __fadd2_rn(x[4 * c + q], mneg);
+        // One pair in eight on the FMA pipe (the kernel is issue-bound more
+        // than MUFU-bound).
+        if (q == 0 && (c & 1) == 0)
+          e = exp2_poly2(e);
+        else
+          e = make_float2(ex2_approx(e.x), ex2_approx(e.y));
+        ps[q] = __ffma2_rn(e, rv[q], ps[q]);
+        const float2 y = __ffma2_rn(e, k255, kb2);
+        uint32_t h = __byte_perm(__float_as_uint(y.x), __float_as_uint(y.y), 0x6420);  // 2 + c/512, twice
+        __half2 pw = __hfma2(*reinterpret_cast<__half2*>(&h), w512, w1024n);
+        words[q] = *reinterpret_cast<uint32_t*>(&pw);
+      }
+      *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
+    }
+    fence_proxy_async_shared();
+    // PV of the previous block must have completed before this block's P is
+    // released, so each pv_full phase is consumed before the next can
+    // complete (and the P buffer of block j + 1 is free).
+    if (j >= 1 && pv_seen < j) {
+      if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
+                                bars.abort_flag)))
+        break;
+      pv_seen = j;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars.p_full + 8 * (t * 2 + buf));
+    const float psum = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
+    l_run = fmaf(psum, w_cur, l_run);
+  }
+  if (ok && nbt > 0) {
+    ok = mbar_wait_warp(bars.pv_full + 8 * t, (nbt - 1) & 1, budget, status, kStatusTimeoutMma, bars.abort_flag);
+    tc_fence_after();
+  }
+
+  // Recomputed here rather than kept live through the loop.
+  const WorkUnit we = decode_unit(p);
+  const int64_t bh_e = we.tile / p.q_tiles;
+  const bool store = we.split >= 0 || (p.state_mode & kStateStore);
+  // Every lane takes part in the TMEM loads (warp-collective); only valid
+  // rows write.
+  if (ok && flag_get(bars.abort_flag) == 0 && (nbt > 0 || load)) {
+    const bool write = valid_row;
+    float4* so = nullptr;
+    uint4* orow = nullptr;
+    const float* vm = p.vmean + bh_e * D;
+    float inv = 0.0f;
+    if (store) {
+      if (we.split >= 0) {
+        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
+        so = reinterpret_cast<float4*>(p.split_state + slot * D);
+        if (write) reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D)[slot] =
+            make_float2(m_ref, l_run);
+      } else {
+        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow) * D);
+        if (write) reinterpret_cast<float2*>(p.state_ml)[bh_e * p.nq_all + grow] = make_float2(m_ref, l_run);
+      }
+    } else {
+      inv = (1.0f / kPScale) / fmaxf(l_run, 1e-30f);
+      orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow) * D);
+    }
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t v[32];
+      __syncwarp();
+      tmem_ld32_split(tm_o + 32 * c, v);
+      tmem_ld_wait();
+      if (!write) {
+      } else if (store) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          so[8 * c + i] = make_float4(__uint_as_float(v[4 * i]) * (1.0f / kPScale),
+                                      __uint_as_float(v[4 * i + 1]) * (1.0f / kPScale),
+                                      __uint_as_float(v[4 * i + 2]) * (1.0f / kPScale),
+                                      __uint_as_float(v[4 * i + 3]) * (1.0f / kPScale));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm + 32 * c) + 2 * i);
+          const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm + 32 * c) + 2 * i + 1);
+          const float* o = reinterpret_cast<const float*>(v) + 8 * i;
+          uint4 pk;
+          pk.x = pack2<T>(fmaf(o[0], inv, m0.x), fmaf(o[1], inv, m0.y));
+          pk.y = pack2<T>(fmaf(o[2], inv, m0.z), fmaf(o[3], inv, m0.w));
+          pk.z = pack2<T>(fmaf(o[4], inv, m1.x), fmaf(o[5], inv, m1.y));
+          pk.w = pack2<T>(fmaf(o[6], inv, m1.z), fmaf(o[7], inv, m1.w));
+          orow[4 * c + i] = pk;
+        }
+      }
+    }
+  } else if (ok && flag_get(bars.abort_flag) == 0 && valid_row) {
+    // No visible key and no carried state: an empty recurrence.
+    if (store) {
+      float4* so;
+      float2* sml;
+      if (we.split >= 0) {
+        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
+        so = reinterpret_cast<float4*>(p.split_state + slot * D);
+        sml = reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D) + slot;
+      } else {
+        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow) * D);
+        sml = reinterpret_cast<float2*>(p.state_ml) + bh_e * p.nq_all + grow;
+      }
+      for (int i = 0; i < D / 4; ++i) so[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      *sml = make_float2(m_ref, l_run);
+    } else {
+      const float* vm = p.vmean + bh_e * D;
+      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow) * D);
+      for (int c = 0; c < D / 8; ++c) {
+        const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);
+        const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c + 1);
+        orow[c] = make_uint4(pack2<T>(m0.x, m0.y), pack2<T>(m0.z, m0.w), pack2<T>(m1.x, m1.y), pack2<T>(m1.z, m1.w));
+      }
+    }
+  }
+}
+
 template <typename T, int D, bool kSage = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     piper_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using S = AttnSmem<D>;
+  using S = AttnSmem<D, !kSage>;
+  constexpr int kStages = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Align to 1024 B (the 128B-swizzle atom) while keeping the pointer derived
   // from the shared array, so every access stays a 32-bit shared access.
@@ -554,11 +850,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint64_t budget = p.wait_budget_ns;
   uint32_t* status = &g_piper_status;
   if (warp < 8) {
-    // Every MMA accumulates onto the bias pattern: arm both S buffers and the
-    // PV accumulator of this thread's lane before the first MMA.
+    // Every QK^T MMA accumulates onto the bias pattern: arm both S buffers of
+    // this thread's lane, and clear (Piper) or arm (SageAttention2++) its PV
+    // accumulator, before the first MMA.
     const uint32_t lane_tm = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16) + (warp / 4) * 256;
     tmem_fill_bias<2 * kKeyBlock>(lane_tm);
-    tmem_fill_bias<D>(lane_tm + 128);
+    if constexpr (kSage) {
+      tmem_fill_bias<D>(lane_tm + 128);
+    } else {
+      // The F32 numerator accumulates from zero.
+#pragma unroll
+      for (int c = 0; c < D; c += 4) tmem_st4_same(lane_tm + 128 + c, 0u);
+    }
     tmem_st_wait();
   }
   tc_fence_before();
@@ -608,14 +911,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // previous fold.  Whatever is ready is issued; a stage is released to
       // the producer once every tile has issued its PV for that block.
       constexpr uint32_t kIdescQK = umma_idesc_i8(true, true, kTileM, kKeyBlock);
-      constexpr uint32_t kIdescPV = umma_idesc_i8(false, true, kTileM, D);
       bool ok = mbar_wait(q_full, 0, budget, status, kStatusTimeoutFull, abort_flag);
       tc_fence_after();
       uint64_t descQ[kTiles];
       for (int t = 0; t < kTiles; ++t) descQ[t] = umma_desc_kmajor(sbase + S::kOffQ + t * S::kQBytes, D);
       const uint64_t descK0 = umma_desc_kmajor(sbase + S::kOffK, D);
-      const uint64_t descV0 = umma_desc_kmajor(sbase + S::kOffV, kKeyBlock);
-      const uint64_t descP0 = umma_desc_kmajor(sbase + S::kOffP, kKeyBlock);
+      const uint64_t descV0 = umma_desc_kmajor(sbase + S::kOffV, S::kPVRow);
+      const uint64_t descP0 = umma_desc_kmajor(sbase + S::kOffP, S::kPVRow);
       int qk_next[kTiles] = {0, 0}, pv_next[kTiles] = {0, 0};
       int released = 0;
       uint64_t idle_since = 0;
@@ -636,8 +938,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             progress = true;
           }
           const int jp = pv_next[t];
+          // Piper accumulates PV in TMEM across blocks: no accumulator to wait for.
           if (jp < qk_next[t] && mbar_test(p_full + 8 * (t * 2 + (jp & 1)), (jp >> 1) & 1) &&
-              mbar_test(pv_free + 8 * t, (jp & 1) ^ 1)) {
+              (!kSage || mbar_test(pv_free + 8 * t, (jp & 1) ^ 1))) {
             tc_fence_after();
             const uint64_t descV = descV0 + static_cast<uint64_t>(((jp % kStages) * S::kVBytes) >> 4);
             const uint64_t descP = descP0 + static_cast<uint64_t>(((t * 2 + (jp & 1)) * S::kPBytes) >> 4);
@@ -648,9 +951,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               for (int kk = 0; kk < kKeyBlock / 32; ++kk)
                 umma_f8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf8, kk > 0 ? 1u : 0u);
             } else {
+              // fp16 weighted probabilities x fp16 V codes, 16 keys (32 B) per
+              // MMA, accumulated in F32 onto the numerator in TMEM.
+              constexpr uint32_t kIdescPVf16 = umma_idesc_f16(kTileM, D);
 #pragma unroll
-              for (int kk = 0; kk < kKeyBlock / 32; ++kk)
-                umma_i8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPV, 1u);
+              for (int kk = 0; kk < kKeyBlock / 16; ++kk)
+                umma_f16(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf16, 1u);
             }
             umma_commit(pv_full + 8 * t);
             pv_next[t] = jp + 1;
@@ -689,211 +995,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sage_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, status, budget);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    // -------------------------------------------------- softmax warpgroups
-    const int t = warp / 4;
-    const int r = threadIdx.x % kTileM;
-    const int row = static_cast<int>(q0) + t * kTileM + r;
-    const bool valid_row = row < p.nq;
-    const int64_t grow = p.q_row0 + row;  // row within the head's nq_all rows
-    const int nbt = nb[t];
-    const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
-    const uint32_t tm_s = tmem_base + lane_base + t * 256;
-    const uint32_t tm_pv = tm_s + 128;
-    const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + grow / kQueryGroup) : 0.0f;
-    const float c_row = qs * p.scale_log2e;
-    const float* kscale = p.kscale + bh * p.k_groups + key0 / kKeyGroup;
-    const float2 nb2 = make_float2(-kBias, -kBias);
-
-    float2 o[D / 2];
-#pragma unroll
-    for (int i = 0; i < D / 2; ++i) o[i] = make_float2(0.0f, 0.0f);
-    // m_ref: reference max of the numerator and denominator (log2 units).
-    // It trails the true running max by less than kRescaleThreshold, which
-    // leaves o/l unchanged and skips almost every rescale.
-    float m_ref = -INFINITY, l_run = 0.0f;
-    float pend_w = 0.0f;  // weight of the PV block awaiting its fold
-    float bias_acc = 0.0f;  // o holds numerator + bias_acc (same FMAs with PV = 0)
-    bool ok = true;
-    // In a split tile only key range 0 continues from the carried state; the
-    // merge combines the ranges.
-    if ((p.state_mode & kStateLoad) && valid_row && split <= 0) {
-      // Continue the recurrence of earlier key shards: the same identity as
-      // a lazy rescale, with the carried reference max.
-      const float4* so = reinterpret_cast<const float4*>(p.state_o + (bh * p.nq_all + grow) * D);
-#pragma unroll
-      for (int i = 0; i < D / 4; ++i) {
-        const float4 v = so[i];
-        o[2 * i] = make_float2(v.x, v.y);
-        o[2 * i + 1] = make_float2(v.z, v.w);
-      }
-      const float2 ml = reinterpret_cast<const float2*>(p.state_ml)[bh * p.nq_all + grow];
-      m_ref = ml.x;
-      l_run = ml.y;
-    }
-
-    for (int j = 0; j < nbt; ++j) {
-      const int s = j % kStages;
-      const int buf = j & 1;
-      const float ks = __ldg(kscale + j);
-      if (!(ok = mbar_wait_warp(kv_full + 8 * (s), (j / kStages) & 1, budget, status, kStatusTimeoutFull, abort_flag)))
-        break;
-      if (!(ok = mbar_wait_warp(s_full + 8 * (t * 2 + buf), (j >> 1) & 1, budget, status, kStatusTimeoutMma, abort_flag)))
-        break;
-      tc_fence_after();
-      float2 x[kKeyBlock / 2];
-      {
-        uint32_t a[32], b[32];
-        tmem_ld32_split(tm_s + buf * kKeyBlock, a);
-        tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
-        tmem_ld_wait();
-        // Re-arm the S buffer; s_free is signalled after the P codes are out,
-        // by which time this store has long completed.
-        tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
-        const float c = c_row * ks;
-        const float2 c2 = make_float2(c, c);
-        const uint32_t vl = sbase + S::kOffVec + s * S::kVecBytes;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 la = lds128(vl + 16 * i), lb = lds128(vl + 16 * (8 + i));
-          x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i], a[4 * i + 1]), nb2), c2, make_float2(la.x, la.y));
-          x[2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2], a[4 * i + 3]), nb2), c2, make_float2(la.z, la.w));
-          x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i], b[4 * i + 1]), nb2), c2, make_float2(lb.x, lb.y));
-          x[16 + 2 * i + 1] =
-              __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2], b[4 * i + 3]), nb2), c2, make_float2(lb.z, lb.w));
-        }
-      }
-      if (p.causal) {
-        // Keys after this row are masked (reference.py:86-91); only the
-        // diagonal block needs work: lim = last visible key - first key of
-        // the block, clamped to [-1, 64].
-        const int lim = static_cast<int>(
-            max(min(static_cast<int64_t>(row) + p.causal_shift - j * kKeyBlock, static_cast<int64_t>(kKeyBlock)),
-                static_cast<int64_t>(-1)));
-        if (lim < kKeyBlock - 1) {
-#pragma unroll
-          for (int i = 0; i < kKeyBlock / 2; ++i) {
-            if (2 * i > lim) x[i].x = -INFINITY;
-            if (2 * i + 1 > lim) x[i].y = -INFINITY;
-          }
-        }
-      }
-      // Block max (reference.py:94-95), four independent 3-input chains.
-      float mx[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) mx[q] = fmaxf(x[q].x, x[q].y);
-#pragma unroll
-      for (int i = 4; i < kKeyBlock / 2; i += 4) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) mx[q] = fmax3(mx[q], x[i + q].x, x[i + q].y);
-      }
-      const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]);
-      // The S buffer was re-armed right after it was read; release it now (the
-      // store has completed behind the max) so QK^T two blocks ahead can start.
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free + 8 * (t * 2 + buf));
-      // Lazy rescale of numerator and denominator (exact identity).
-      const bool need = mb > m_ref + kRescaleThreshold;
-      if (__any_sync(0xffffffffu, need)) {
-        const float new_ref = need ? mb : m_ref;
-        const float w_old = ex2_approx(m_ref - new_ref);
-        const float2 w2 = make_float2(w_old, w_old);
-#pragma unroll
-        for (int i = 0; i < D / 2; ++i) o[i] = __fmul2_rn(o[i], w2);
-        l_run *= w_old;
-        pend_w *= w_old;
-        bias_acc *= w_old;
-        m_ref = new_ref;
-      }
-      // Probabilities relative to the block max: e = p * vs in [0,1]
-      // (reference.py:99, 104-108); UINT8 codes round(255 e) half-to-even.
-      const float m_use = (mb == -INFINITY) ? 0.0f : mb;
-      const float2 mneg = make_float2(-m_use, -m_use);
-      const uint32_t vr = sbase + S::kOffVec + s * S::kVecBytes + kKeyBlock * 4;
-      float2 ps[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
-                      make_float2(0.0f, 0.0f)};
-      const float2 k255 = make_float2(255.0f, 255.0f);
-      const float2 kb2 = make_float2(kBias, kBias);
-      uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * kKeyBlock;
-      const int sw = (r >> 1) & 3;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t words[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int w = 4 * c + q;
-          const float4 rv = lds128(vr + 16 * w);
-          float2 e0 = __fadd2_rn(x[2 * w], mneg);
-          float2 e1 = __fadd2_rn(x[2 * w + 1], mneg);
-          e0 = make_float2(ex2_approx(e0.x), ex2_approx(e0.y));
-          // One pair in eight on the FMA pipe (measured best: 1/4 and 1/2 are
-          // slower, the kernel is issue-bound more than MUFU-bound).
-          if (q == 0)
-            e1 = exp2_poly2(e1);
-          else
-            e1 = make_float2(ex2_approx(e1.x), ex2_approx(e1.y));
-          ps[q] = __ffma2_rn(e0, make_float2(rv.x, rv.y), ps[q]);
-          ps[q] = __ffma2_rn(e1, make_float2(rv.z, rv.w), ps[q]);
-          const float2 y0 = __ffma2_rn(e0, k255, kb2);
-          const float2 y1 = __ffma2_rn(e1, k255, kb2);
-          words[q] = __byte_perm(__byte_perm(__float_as_uint(y0.x), __float_as_uint(y0.y), 0x0040),
-                                 __byte_perm(__float_as_uint(y1.x), __float_as_uint(y1.y), 0x0040), 0x5410);
-        }
-        *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
-      }
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + 8 * (t * 2 + buf));
-      const float psum = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
-      const float w_cur = (mb == -INFINITY) ? 0.0f : ex2_approx(mb - m_ref);
-      l_run = fmaf(psum, w_cur, l_run);
-      if (j >= 1 &&
-          !(ok = fold_pv<D>(o, pv_full + 8 * (t), pv_free + 8 * (t), j - 1, tm_pv, pend_w, lane, budget, status, abort_flag)))
-        break;
-      if (j >= 1) bias_acc = fmaf(kBias, pend_w, bias_acc);
-      pend_w = w_cur * (1.0f / 255.0f);
-    }
-    if (ok && nbt > 0)
-      ok = fold_pv<D>(o, pv_full + 8 * (t), pv_free + 8 * (t), nbt - 1, tm_pv, pend_w, lane, budget, status, abort_flag);
-    bias_acc = fmaf(kBias, pend_w, bias_acc);
-
-    // Recomputed here rather than kept live through the loop.
-    const WorkUnit we = decode_unit(p);
-    const int64_t bh_e = we.tile / p.q_tiles;
-    const int64_t grow_e = p.q_row0 + row;
-    if (ok && valid_row && flag_get(abort_flag) == 0 && (we.split >= 0 || (p.state_mode & kStateStore))) {
-      float4* so;
-      float2* sml;
-      if (we.split >= 0) {
-        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
-        so = reinterpret_cast<float4*>(p.split_state + slot * D);
-        sml = reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D) + slot;
-      } else {
-        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow_e) * D);
-        sml = reinterpret_cast<float2*>(p.state_ml) + bh_e * p.nq_all + grow_e;
-      }
-#pragma unroll
-      for (int i = 0; i < D / 4; ++i)
-        so[i] = make_float4(o[2 * i].x - bias_acc, o[2 * i].y - bias_acc, o[2 * i + 1].x - bias_acc,
-                            o[2 * i + 1].y - bias_acc);
-      *sml = make_float2(m_ref, l_run);
-    } else if (ok && valid_row && flag_get(abort_flag) == 0) {
-      const float inv = 1.0f / fmaxf(l_run, 1e-30f);
-      const float* vm = p.vmean + bh_e * D;
-      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow_e) * D);
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);
-        const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c + 1);
-        uint4 pk;
-        pk.x = pack2<T>(fmaf(o[4 * c].x - bias_acc, inv, m0.x), fmaf(o[4 * c].y - bias_acc, inv, m0.y));
-        pk.y = pack2<T>(fmaf(o[4 * c + 1].x - bias_acc, inv, m0.z), fmaf(o[4 * c + 1].y - bias_acc, inv, m0.w));
-        pk.z = pack2<T>(fmaf(o[4 * c + 2].x - bias_acc, inv, m1.x), fmaf(o[4 * c + 2].y - bias_acc, inv, m1.y));
-        pk.w = pack2<T>(fmaf(o[4 * c + 3].x - bias_acc, inv, m1.z), fmaf(o[4 * c + 3].y - bias_acc, inv, m1.w));
-        orow[c] = pk;
-      }
-    }
+    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag};
+    piper_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
   }
 
   __syncwarp();

@@ -8,7 +8,8 @@
 //   -- K/V pack: k8 .. vrcp are one contiguous span (kv_pack, kv_pack_bytes),
 //      the unit a sequence-sharded ring passes from rank to rank --
 //   k8      int8  [BH, Nk, D]                 centered-K codes (per-64-row scale)
-//   v8t     int8  [BH, D, Nk_pad]             V codes transposed: keys contiguous
+//   v8t     f16   [BH, D, Nk_pad]             V codes (the INT8 values, exact in fp16)
+//                                             transposed: keys contiguous
 //   kscale  f32   [BH, ceil(Nk/64)]           K group scales   (reference: key_scale)
 //   vscale  f32   [BH, Nk_pad]                V row scales     (reference: value_scale)
 //   vlog2   f32   [BH, Nk_pad]                log2(vscale); -inf on padded keys
@@ -57,7 +58,7 @@ inline piper_b200_workspace_layout_t make_layout(int64_t bh, int64_t nq, int64_t
   L.q8 = take(static_cast<uint64_t>(bh * nq * d));
   L.qscale = take(static_cast<uint64_t>(bh * L.q_groups) * 4);
   L.k8 = take(static_cast<uint64_t>(bh * nk * d));
-  L.v8t = take(static_cast<uint64_t>(bh * d * L.nk_pad));
+  L.v8t = take(static_cast<uint64_t>(bh * d * L.nk_pad) * 2);
   L.kscale = take(static_cast<uint64_t>(bh * L.k_groups) * 4);
   L.vscale = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);
   L.vlog2 = take(static_cast<uint64_t>(bh * L.nk_pad) * 4);

@@ -85,7 +85,9 @@ int ensure_device(int* device_out) {
                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>),
                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>)};
   for (int i = 0; i < 8; ++i) {
-    const int smem_bytes = (i % 2 == 0) ? piper::AttnSmem<64>::kAlloc : piper::AttnSmem<128>::kAlloc;
+    // Piper kernels (i < 4) stage 16-bit PV operands; SageAttention2++ 8-bit ones.
+    const int smem_bytes = i < 4 ? ((i % 2 == 0) ? piper::AttnSmem<64, true>::kAlloc : piper::AttnSmem<128, true>::kAlloc)
+                                 : ((i % 2 == 0) ? piper::AttnSmem<64>::kAlloc : piper::AttnSmem<128>::kAlloc);
     PIPER_CUDA(cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
     cudaFuncAttributes attr;
     PIPER_CUDA(cudaFuncGetAttributes(&attr, kernels[i]));
@@ -102,17 +104,21 @@ int ensure_device(int* device_out) {
   return PIPER_B200_OK;
 }
 
-// 3-D int8 tensor map: dims {inner, mid, outer} with byte strides
-// {mid_stride, outer_stride}, a box {box_inner, box_mid, 1} and the swizzle
-// matching box_inner (64 or 128 bytes).
+// 3-D tensor map of 1- or 2-byte elements: dims {inner, mid, outer} in
+// elements with byte strides {mid_stride, outer_stride}, a box {box_inner,
+// box_mid, 1} and the swizzle matching the box's inner extent in bytes (64 or
+// 128).
 int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t mid, uint64_t outer,
-               uint64_t mid_stride, uint64_t outer_stride, uint32_t box_inner, uint32_t box_mid) {
+               uint64_t mid_stride, uint64_t outer_stride, uint32_t box_inner, uint32_t box_mid,
+               int elem_bytes = 1) {
   const cuuint64_t dims[3] = {inner, mid, outer};
   const cuuint64_t strides[2] = {mid_stride, outer_stride};
   const cuuint32_t box[3] = {box_inner, box_mid, 1};
   const cuuint32_t elem[3] = {1, 1, 1};
-  const CUtensorMapSwizzle sw = box_inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+  const CUtensorMapSwizzle sw =
+      box_inner * elem_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapDataType type = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUresult r = g_encode(map, type, 3, const_cast<void*>(base), dims, strides, box,
                               elem, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(PIPER_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
@@ -266,8 +272,9 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   if ((rc = encode_map(&tmK, kv + L.k8, d, nk_all, bh, d, nk_all * d, static_cast<uint32_t>(d), piper::kKeyBlock)) !=
       PIPER_B200_OK)
     return rc;
-  if ((rc = encode_map(&tmV, kv + L.v8t, L.nk_pad, d, bh, L.nk_pad, L.nk_pad * d, piper::kKeyBlock,
-                       static_cast<uint32_t>(d))) != PIPER_B200_OK)
+  // V codes are fp16: rows of nk_pad elements (2 bytes each).
+  if ((rc = encode_map(&tmV, kv + L.v8t, L.nk_pad, d, bh, L.nk_pad * 2, L.nk_pad * d * 2, piper::kKeyBlock,
+                       static_cast<uint32_t>(d), 2)) != PIPER_B200_OK)
     return rc;
   piper::AttnParams p{};
   p.qscale = reinterpret_cast<const float*>(ws + L.qscale);
@@ -322,18 +329,18 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   constexpr unsigned kMergeThreads = piper::kTileM * piper::kTiles;
   if (dtype == PIPER_B200_FLOAT16) {
     if (head_dim == 64) {
-      piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__half, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
     } else {
-      piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__half, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
     }
   } else {
     if (head_dim == 64) {
-      piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
     } else {
-      piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
     }
   }
@@ -345,7 +352,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
 
 extern "C" {
 
-int piper_b200_abi_version(void) { return 102; }
+int piper_b200_abi_version(void) { return 103; }
 
 const char* piper_b200_last_error(void) { return g_last_error.c_str(); }
 

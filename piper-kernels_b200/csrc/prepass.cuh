@@ -270,6 +270,19 @@ __device__ __forceinline__ uint2 pack_codes(const float (&x)[8], float s, float 
 // codes go row-major into a padded shared tile (row stride D/4+1 words, so
 // rows fall on distinct banks), then are transposed 4x4 bytes at a time with
 // byte permutes and written as [D, keys] with coalesced 4-byte stores.
+// Four INT8 codes (one per byte) to four fp16 values, exactly: byte b holds
+// c; (c + 128) placed under the fp16 exponent of 1024 reads as 1152 + c, and
+// one packed subtraction leaves c.
+__device__ __forceinline__ uint2 codes_to_f16x4(uint32_t w) {
+  const uint32_t u = w ^ 0x80808080u;  // c + 128 in each byte
+  const __half2 k = __halves2half2(__float2half_rn(1152.0f), __float2half_rn(1152.0f));
+  uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140);  // halves 0x64:(c0+128), 0x64:(c1+128)
+  uint32_t hi = __byte_perm(u, 0x64646464u, 0x5342);
+  __half2 a = __hsub2(*reinterpret_cast<__half2*>(&lo), k);
+  __half2 b = __hsub2(*reinterpret_cast<__half2*>(&hi), k);
+  return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
 template <typename T, int D, bool kVec16>
 __global__ void __launch_bounds__(kPrepassThreads) quantize_kernel(PrepassArgs a) {
   constexpr int kVpr = D / 8;                   // 16-byte vectors per row
@@ -426,9 +439,10 @@ __global__ void __launch_bounds__(kPrepassThreads) quantize_kernel(PrepassArgs a
     }
   }
   __syncthreads();
-  // ---- transpose to [D, keys]: each step moves a 4-key x 4-feature block.
+  // ---- transpose to [D, keys]: each step moves a 4-key x 4-feature block;
+  // the codes are stored as fp16 (the attention kernel's PV operand).
   {
-    uint32_t* v8t = reinterpret_cast<uint32_t*>(a.ws + L.v8t);
+    uint2* v16t = reinterpret_cast<uint2*>(a.ws + L.v8t);
     constexpr int kBlocks = (D / 4) * (kKeyBlock / 4);
 #pragma unroll
     for (int blk = tid; blk < kBlocks; blk += kPrepassThreads) {
@@ -442,10 +456,10 @@ __global__ void __launch_bounds__(kPrepassThreads) quantize_kernel(PrepassArgs a
       const uint32_t t2 = __byte_perm(w0, w1, 0x7362), t3 = __byte_perm(w2, w3, 0x7362);
       const uint32_t o[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632), __byte_perm(t2, t3, 0x5410),
                              __byte_perm(t2, t3, 0x7632)};
-      // word index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and row0 are multiples of 64.
+      // 8-byte index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and row0 are multiples of 64.
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        v8t[((bh * D + 4 * dq + j) * L.nk_pad + row0) / 4 + kq] = o[j];
+        v16t[((bh * D + 4 * dq + j) * L.nk_pad + row0) / 4 + kq] = codes_to_f16x4(o[j]);
     }
   }
 }

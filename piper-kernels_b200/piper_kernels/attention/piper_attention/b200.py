@@ -40,7 +40,8 @@ class PreparedPiperAttention:
 
     The views alias ``workspace``; they match the reference's prepared tensors
     (triton.py:754-769) except that V codes are stored transposed
-    ``[B,H,D,Nk_pad]`` and scales are per group (``[B,H,ceil(N/32|64)]``).
+    ``[B,H,D,Nk_pad]`` as fp16 (the INT8 values exactly; the INT8 views are
+    converted copies) and scales are per group (``[B,H,ceil(N/32|64)]``).
     """
 
     workspace: torch.Tensor
@@ -64,10 +65,16 @@ class PreparedPiperAttention:
         return self._view(self.layout.k8, b * h * nk * d, torch.int8, (b, h, nk, d))
 
     @property
-    def value_int8_transposed(self) -> torch.Tensor:
+    def value_f16_transposed(self) -> torch.Tensor:
+        """``[B,H,D,Nk_pad]`` V codes as stored for the fp16 PV MMA (exact INT8 values)."""
         b, h, _nq, _nk, d = self.shape
         pad = self.layout.nk_pad
-        return self._view(self.layout.v8t, b * h * d * pad, torch.int8, (b, h, d, pad))
+        return self._view(self.layout.v8t, b * h * d * pad, torch.float16, (b, h, d, pad))
+
+    @property
+    def value_int8_transposed(self) -> torch.Tensor:
+        """``[B,H,D,Nk_pad]`` INT8 V codes (a copy of the fp16 store, exactly converted)."""
+        return self.value_f16_transposed.to(torch.int8)
 
     @property
     def value_int8(self) -> torch.Tensor:

@@ -44,6 +44,9 @@ def _check_against_oracle(q, k, v, is_causal) -> None:
     vt = prepared.value_int8_transposed.cpu()
     nk = k.shape[2]
     assert not vt[..., nk:].any(), "padded keys must hold zero codes"
+    # The stored operand is fp16 and must hold the INT8 codes exactly.
+    vf = prepared.value_f16_transposed.cpu().float()
+    assert torch.equal(vf, vt.float())
 
 
 @pytest.mark.parametrize("name", golden_cases())

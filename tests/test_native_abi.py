@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol() -> None:
 
 
 def test_abi_version() -> None:
-    assert _native.library().piper_b200_abi_version() == 102
+    assert _native.library().piper_b200_abi_version() == 103
 
 
 def test_workspace_layout_regions_are_aligned_and_disjoint() -> None:
@@ -41,7 +41,7 @@ def test_workspace_layout_regions_are_aligned_and_disjoint() -> None:
         bh = b * h
         regions = [
             (L.q8, bh * nq * d), (L.qscale, bh * L.q_groups * 4),
-            (L.k8, bh * nk * d), (L.v8t, bh * d * L.nk_pad), (L.kscale, bh * L.k_groups * 4),
+            (L.k8, bh * nk * d), (L.v8t, bh * d * L.nk_pad * 2), (L.kscale, bh * L.k_groups * 4),
             (L.vscale, bh * L.nk_pad * 4), (L.vlog2, bh * L.nk_pad * 4), (L.vrcp, bh * L.nk_pad * 4),
             (L.kmean, bh * d * 4), (L.vmean, bh * d * 4), (L.totals, 2 * bh * d * 8),
             (L.ksum, bh * L.chunks * d * 8), (L.vsum, bh * L.chunks * d * 8), (L.counter, bh * 4),
