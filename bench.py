@@ -374,7 +374,9 @@ def run_b200(args) -> None:
     peak_note = "2 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json)" if bf16_peak else "2 x fallback 1.59 PF bf16"
     attn_tops = ops_rank / (attn_avg_ms * 1e-3) / 1e12
     hbm = measured.get("hbm_gbs") or 6650.0
-    prepass_bytes = b * h * n * d * (3 * 2 + 3) + b * h * (n // 32 + n // 64 + 3 * n) * 4
+    # Read Q, K, V once (2 B each); write INT8 Q and K codes and the fp16 V codes
+    # (1 + 1 + 2 B); plus the scales and per-key vectors.
+    prepass_bytes = b * h * n * d * (3 * 2 + 4) + b * h * (n // 32 + n // 64 + 3 * n) * 4
     if rank == 0:
         line = {
             "metric": METRIC,

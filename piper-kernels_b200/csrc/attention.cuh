@@ -157,9 +157,9 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// TMEM accumulators are pre-loaded with the bit pattern of 1.5*2^23 before
-// every MMA chain (which accumulates onto it), so an INT32 result v with
-// |v| < 2^22 reads back as the float 1.5*2^23 + v exactly: one packed
+// The TMEM score accumulators are pre-loaded with the bit pattern of 1.5*2^23
+// before every QK^T chain (which accumulates onto it), so an INT32 result v
+// with |v| < 2^22 reads back as the float 1.5*2^23 + v exactly: one packed
 // subtraction converts two values.
 constexpr uint32_t kBiasBits = 0x4B400000u;
 constexpr float kBias = 12582912.0f;
