@@ -12,7 +12,7 @@ collective on the data path); the reported time is the max over ranks.
 
 ``--workload c5`` (B1 H24 N131072) splits the sequence
 over the ranks instead (strong scaling): one step is a whole
-``ring_piper_attention`` call, with the INT8 K/V packs passed around an NCCL
+``ring_piper_attention`` call, with the quantized K/V packs passed around an NCCL
 ring and the fp64 column totals all-reduced.
 
 Metric: TOPS = 4*B*H*Nq*Nk*D / t (the reference's formula,
@@ -590,7 +590,7 @@ def run_ring(args) -> None:
                 "seq_len": n,
                 "head_dim": d,
                 "causal": causal,
-                "parallelism": (f"sequence ring x{world}: NCCL send/recv of INT8 K/V packs "
+                "parallelism": (f"sequence ring x{world}: NCCL send/recv of K/V code packs "
                                 f"({shard} keys per rank), all-reduce of fp64 [2,B,H,D] column totals"),
                 "l2": "inputs larger than L2 (Q/K/V shard of one rank = %.0f MB)" % (3 * b * h * shard * d * 2 / 1e6),
             },
