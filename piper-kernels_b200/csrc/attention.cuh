@@ -637,9 +637,10 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float2 e = __fadd2_rn(x[4 * c + q], mneg);
-        // One pair in eight on the FMA pipe (the kernel is issue-bound more
-        // than MUFU-bound).
-        if (q == 0 && (c & 1) == 0)
+        // At D=64 one pair in eight goes to the FMA pipe; at D=128 the PV
+        // MMA's longer shadow leaves the MUFU enough time (measured: the
+        // polynomial share costs 2% there and gains 7% at D=64).
+        if (D == 64 && q == 0 && (c & 1) == 0)
           e = exp2_poly2(e);
         else
           e = make_float2(ex2_approx(e.x), ex2_approx(e.y));
