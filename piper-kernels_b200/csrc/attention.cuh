@@ -240,43 +240,14 @@ __device__ __forceinline__ WorkUnit decode_unit(const AttnParams& p) {
 //   l      = l*2^(m-m') + sum_k p_k
 //   O      = O*2^(m-m') + (P8 . V8)         e4m3 x e4m3 -> F32 on the tensor core
 //   out    = O * vscale / max(l, 1e-30)
-// The 64-key partial is accumulated in F32; the reference rounds it to fp16
-// first (the FP16-accumulating MMA it emulates), a difference at the fp16
-// rounding level.  The per-key K scale and the padded-key mask arrive through
-// the producer's two per-key vector slots.
+// The numerator is accumulated in F32 in TMEM across the blocks; the
+// reference rounds each 64-key partial to fp16 first (the FP16-accumulating
+// MMA it emulates), a difference at the fp16 rounding level.  The per-key K
+// scale and the padded-key mask arrive through the producer's two per-key
+// vector slots.
 struct SoftmaxBars {
   uint32_t kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag;
 };
-
-// Folds the F32 PV partial of block jj: o += PV * w; the accumulator is
-// released as soon as its last columns are in registers (the next chain
-// overwrites it).
-template <int D>
-__device__ __forceinline__ bool fold_pv_f32(float2 (&o)[D / 2], uint32_t full, uint32_t free_bar, int jj,
-                                            uint32_t tm_pv, float w, int lane, uint64_t budget, uint32_t* status,
-                                            uint32_t abort_flag) {
-  if (!mbar_wait_warp(full, jj & 1, budget, status, kStatusTimeoutMma, abort_flag)) return false;
-  tc_fence_after();
-  const float2 w2 = make_float2(w, w);
-#pragma unroll
-  for (int c = 0; c < D / 64; ++c) {
-    uint32_t v0[32], v1[32];
-    tmem_ld32_split(tm_pv + c * 64, v0);
-    tmem_ld32_split(tm_pv + c * 64 + 32, v1);
-    tmem_ld_wait();
-    if (c == D / 64 - 1) {
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(free_bar);
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[c * 32 + i] = __ffma2_rn(f2(v0[2 * i], v0[2 * i + 1]), w2, o[c * 32 + i]);
-      o[c * 32 + 16 + i] = __ffma2_rn(f2(v1[2 * i], v1[2 * i + 1]), w2, o[c * 32 + 16 + i]);
-    }
-  }
-  return true;
-}
 
 __device__ __forceinline__ uint32_t e4m3x4(float2 a, float2 b) {
   uint32_t lo, hi;
@@ -287,6 +258,35 @@ __device__ __forceinline__ uint32_t e4m3x4(float2 a, float2 b) {
   return __byte_perm(lo, hi, 0x5410);
 }
 
+// Scales this thread's numerator row in TMEM (D columns) by w, 32 at a time.
+template <int D>
+__device__ __forceinline__ void tmem_scale_row(uint32_t tm_o, float w) {
+  const float2 w2 = make_float2(w, w);
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t v[32];
+    tmem_ld32_split(tm_o + 32 * c, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 y = __fmul2_rn(f2(v[2 * i], v[2 * i + 1]), w2);
+      v[2 * i] = __float_as_uint(y.x);
+      v[2 * i + 1] = __float_as_uint(y.y);
+    }
+    tmem_st8(tm_o + 32 * c, v);
+    tmem_st8(tm_o + 32 * c + 8, v + 8);
+    tmem_st8(tm_o + 32 * c + 16, v + 16);
+    tmem_st8(tm_o + 32 * c + 24, v + 24);
+  }
+  tmem_st_wait();
+}
+
+// The numerator accumulates in F32 in TMEM across all blocks (the PV MMAs of
+// every block add onto it); when a row's running max rises, the warp scales
+// its rows there once the PV MMAs issued so far have completed.  Each block
+// consumes the previous block's PV completion before releasing its own P, so
+// every pv_full parity wait is unambiguous and the P buffer a block writes
+// (last read by PV(j - 2)) is free.
 template <typename T, int D>
 __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* smem, uint32_t sbase,
                                                   uint32_t tmem_base, const SoftmaxBars& bars, int nbt, int64_t q0,
@@ -300,16 +300,14 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
   const bool valid_row = row < p.nq;
   const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
   const uint32_t tm_s = tmem_base + lane_base + t * 256;
-  const uint32_t tm_pv = tm_s + 128;
+  const uint32_t tm_o = tm_s + 128;
   const float qs = valid_row ? __ldg(p.qscale + bh * p.nq_all + p.q_row0 + row) : 0.0f;
   const float c_row = qs * p.scale_log2e;
   const float2 c2 = make_float2(c_row, c_row);
   const float2 nb2 = make_float2(-kBias, -kBias);
-  float2 o[D / 2];
-#pragma unroll
-  for (int i = 0; i < D / 2; ++i) o[i] = make_float2(0.0f, 0.0f);
-  float m_run = -INFINITY, l_run = 0.0f, pend_w = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
   bool ok = true;
+  int pv_seen = 0;  // pv_full completions consumed (one per block)
   for (int j = 0; j < nbt; ++j) {
     const int s = j % S::kStages;
     const int buf = j & 1;
@@ -369,7 +367,7 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
     __syncwarp();
     if (lane == 0) mbar_arrive(bars.s_free + 8 * (t * 2 + buf));
     // Running max, shifted by log2(448) (reference.py:83-86): rescale the
-    // numerator, the denominator and the partial awaiting its fold.
+    // numerator (in TMEM, after the earlier PV MMAs) and the denominator.
     const float msh = mb - kLog2FP8Max;
     const bool need = msh > m_run;
     if (__any_sync(0xffffffffu, need)) {
@@ -377,11 +375,15 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
       // Lanes that keep their maximum scale by exactly 1 (also when it is
       // still -inf, where the difference would be NaN).
       const float w_old = need ? ex2_approx(m_run - m_new) : 1.0f;
-      const float2 w2 = make_float2(w_old, w_old);
-#pragma unroll
-      for (int i = 0; i < D / 2; ++i) o[i] = __fmul2_rn(o[i], w2);
+      if (j >= 1) {
+        if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
+                                  bars.abort_flag)))
+          break;
+        pv_seen = j;
+        tc_fence_after();
+        tmem_scale_row<D>(tm_o, w_old);
+      }
       l_run *= w_old;
-      pend_w *= w_old;
       m_run = m_new;
     }
     const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
@@ -409,31 +411,45 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
       *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
     }
     fence_proxy_async_shared();
+    // PV(j - 1) completes before P(j) is released (one pv_full phase per block).
+    if (j >= 1 && pv_seen < j) {
+      if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
+                                bars.abort_flag)))
+        break;
+      pv_seen = j;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(bars.p_full + 8 * (t * 2 + buf));
     l_run += ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
-    if (j >= 1 && !(ok = fold_pv_f32<D>(o, bars.pv_full + 8 * t, bars.pv_free + 8 * t, j - 1, tm_pv, pend_w, lane,
-                                        budget, status, bars.abort_flag)))
-      break;
-    pend_w = 1.0f;
   }
-  if (ok && nbt > 0)
-    ok = fold_pv_f32<D>(o, bars.pv_full + 8 * t, bars.pv_free + 8 * t, nbt - 1, tm_pv, pend_w, lane, budget, status,
-                        bars.abort_flag);
-  if (ok && valid_row && flag_get(bars.abort_flag) == 0) {
+  if (ok && nbt > 0) {
+    ok = mbar_wait_warp(bars.pv_full + 8 * t, (nbt - 1) & 1, budget, status, kStatusTimeoutMma, bars.abort_flag);
+    tc_fence_after();
+  }
+  if (ok && flag_get(bars.abort_flag) == 0 && nbt > 0) {
     const float inv = 1.0f / fmaxf(l_run, 1e-30f);
     const float* vs = p.vmean + bh * D;  // per-channel V scale
     uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + p.q_row0 + row) * D);
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t v[32];
+      __syncwarp();
+      tmem_ld32_split(tm_o + 32 * c, v);
+      tmem_ld_wait();
+      if (valid_row) {
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const float4 s0 = __ldg(reinterpret_cast<const float4*>(vs) + 2 * c);
-      const float4 s1 = __ldg(reinterpret_cast<const float4*>(vs) + 2 * c + 1);
-      uint4 pk;
-      pk.x = pack2<T>(o[4 * c].x * s0.x * inv, o[4 * c].y * s0.y * inv);
-      pk.y = pack2<T>(o[4 * c + 1].x * s0.z * inv, o[4 * c + 1].y * s0.w * inv);
-      pk.z = pack2<T>(o[4 * c + 2].x * s1.x * inv, o[4 * c + 2].y * s1.y * inv);
-      pk.w = pack2<T>(o[4 * c + 3].x * s1.z * inv, o[4 * c + 3].y * s1.w * inv);
-      orow[c] = pk;
+        for (int i = 0; i < 4; ++i) {
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(vs + 32 * c) + 2 * i);
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(vs + 32 * c) + 2 * i + 1);
+          const float* o = reinterpret_cast<const float*>(v) + 8 * i;
+          uint4 pk;
+          pk.x = pack2<T>(o[0] * s0.x * inv, o[1] * s0.y * inv);
+          pk.y = pack2<T>(o[2] * s0.z * inv, o[3] * s0.w * inv);
+          pk.z = pack2<T>(o[4] * s1.x * inv, o[5] * s1.y * inv);
+          pk.w = pack2<T>(o[6] * s1.z * inv, o[7] * s1.w * inv);
+          orow[4 * c + i] = pk;
+        }
+      }
     }
   }
 }
@@ -852,17 +868,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint32_t* status = &g_piper_status;
   if (warp < 8) {
     // Every QK^T MMA accumulates onto the bias pattern: arm both S buffers of
-    // this thread's lane, and clear (Piper) or arm (SageAttention2++) its PV
-    // accumulator, before the first MMA.
+    // this thread's lane, and clear its numerator, before the first MMA.
     const uint32_t lane_tm = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16) + (warp / 4) * 256;
     tmem_fill_bias<2 * kKeyBlock>(lane_tm);
-    if constexpr (kSage) {
-      tmem_fill_bias<D>(lane_tm + 128);
-    } else {
-      // The F32 numerator accumulates from zero.
+    // The F32 numerator accumulates from zero.
 #pragma unroll
-      for (int c = 0; c < D; c += 4) tmem_st4_same(lane_tm + 128 + c, 0u);
-    }
+    for (int c = 0; c < D; c += 4) tmem_st4_same(lane_tm + 128 + c, 0u);
     tmem_st_wait();
   }
   tc_fence_before();
@@ -939,9 +950,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             progress = true;
           }
           const int jp = pv_next[t];
-          // Piper accumulates PV in TMEM across blocks: no accumulator to wait for.
-          if (jp < qk_next[t] && mbar_test(p_full + 8 * (t * 2 + (jp & 1)), (jp >> 1) & 1) &&
-              (!kSage || mbar_test(pv_free + 8 * t, (jp & 1) ^ 1))) {
+          // PV accumulates in TMEM across blocks: no accumulator to wait for.
+          if (jp < qk_next[t] && mbar_test(p_full + 8 * (t * 2 + (jp & 1)), (jp >> 1) & 1)) {
             tc_fence_after();
             const uint64_t descV = descV0 + static_cast<uint64_t>(((jp % kStages) * S::kVBytes) >> 4);
             const uint64_t descP = descP0 + static_cast<uint64_t>(((t * 2 + (jp & 1)) * S::kPBytes) >> 4);
@@ -950,7 +960,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               constexpr uint32_t kIdescPVf8 = umma_idesc_e4m3(kTileM, D);
 #pragma unroll
               for (int kk = 0; kk < kKeyBlock / 32; ++kk)
-                umma_f8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf8, kk > 0 ? 1u : 0u);
+                umma_f8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf8, 1u);
             } else {
               // fp16 weighted probabilities x fp16 V codes, 16 keys (32 B) per
               // MMA, accumulated in F32 onto the numerator in TMEM.
