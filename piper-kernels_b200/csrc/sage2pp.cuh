@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kPrepassThreads) sage_stats_kernel(SagePrepass
 
 // ---------------------------------------------------------------------------
 template <typename T, int D, bool kVec16>
-__global__ void __launch_bounds__(kPrepassThreads) sage_quantize_kernel(SagePrepassArgs a) {
+__global__ void __launch_bounds__(kPrepassThreads, 3) sage_quantize_kernel(SagePrepassArgs a) {
   constexpr int kVpr = D / 8;                   // threads per row (consecutive lanes)
   constexpr int kRpp = kPrepassThreads / kVpr;  // rows per pass
   constexpr int kPasses = kKeyBlock / kRpp;
