@@ -90,7 +90,7 @@ struct AttnSmem {
   static constexpr int kOffP = kOffV + kStages * kVBytes;
   static constexpr int kOffVec = kOffP + kTiles * 2 * kPBytes;
   static constexpr int kOffBar = kOffVec + kStages * kVecBytes;
-  static constexpr int kNumBars = 1 + 2 * kStages + 3 * kTiles * 2 + 2 * kTiles + 1;
+  static constexpr int kNumBars = 1 + 2 * kStages + 3 * kTiles * 2 + kTiles + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
@@ -246,7 +246,7 @@ __device__ __forceinline__ WorkUnit decode_unit(const AttnParams& p) {
 // scale and the padded-key mask arrive through the producer's two per-key
 // vector slots.
 struct SoftmaxBars {
-  uint32_t kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag;
+  uint32_t kv_full, s_full, s_free, p_full, pv_full, abort_flag;
 };
 
 __device__ __forceinline__ uint32_t e4m3x4(float2 a, float2 b) {
@@ -791,8 +791,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t s_free = s_full + 8 * kTiles * 2;        // [tile][buf]
   const uint32_t p_full = s_free + 8 * kTiles * 2;        // [tile][buf]
   const uint32_t pv_full = p_full + 8 * kTiles * 2;       // [tile]
-  const uint32_t pv_free = pv_full + 8 * kTiles;          // [tile]
-  const uint32_t mma_done = pv_free + 8 * kTiles;
+  const uint32_t mma_done = pv_full + 8 * kTiles;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffMisc);
   const uint32_t abort_flag = sbase + S::kOffMisc + 4;
 
@@ -845,7 +844,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(pv_full + 8 * t, 1);
-      mbar_init(pv_free + 8 * t, 4);
     }
     mbar_init(mma_done, 1);
     flag_set(abort_flag, 0u);
@@ -919,9 +917,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // ------------------------------------------------ MMA issuer
       // Event driven: each tile advances on its own.  QK^T of block j needs
       // the K/V stage loaded and the S buffer released by the softmax; PV of
-      // block j needs the P codes and the PV accumulator released by the
-      // previous fold.  Whatever is ready is issued; a stage is released to
-      // the producer once every tile has issued its PV for that block.
+      // block j needs its P (it accumulates onto the numerator in TMEM).
+      // Whatever is ready is issued; a stage is released to the producer once
+      // every tile has issued its PV for that block.
       constexpr uint32_t kIdescQK = umma_idesc_i8(true, true, kTileM, kKeyBlock);
       bool ok = mbar_wait(q_full, 0, budget, status, kStatusTimeoutFull, abort_flag);
       tc_fence_after();
@@ -1002,11 +1000,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if constexpr (kSage) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag};
+    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, abort_flag};
     sage_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, status, budget);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, pv_free, abort_flag};
+    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, abort_flag};
     piper_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
   }
 
