@@ -454,6 +454,29 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
   }
 }
 
+// x = S*c + log2(vs_k) for the 64 scores of a block (two packed f32 per
+// pair of keys).  The INT32 scores read as floats 1.5*2^23 + S either because
+// the accumulator was pre-biased (kAddBias false) or because the bias bits
+// are added here as integers to a score accumulated from zero (kAddBias
+// true); one packed subtraction then leaves S exactly.
+template <bool kAddBias>
+__device__ __forceinline__ void scores_to_x(const uint32_t (&a)[32], const uint32_t (&b)[32], float2 (&x)[32],
+                                            float c, uint32_t vl) {
+  const uint32_t add = kAddBias ? kBiasBits : 0u;
+  const float2 c2 = make_float2(c, c);
+  const float2 nb2 = make_float2(-kBias, -kBias);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 la = lds128(vl + 16 * i), lb = lds128(vl + 16 * (8 + i));
+    x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i] + add, a[4 * i + 1] + add), nb2), c2, make_float2(la.x, la.y));
+    x[2 * i + 1] =
+        __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2] + add, a[4 * i + 3] + add), nb2), c2, make_float2(la.z, la.w));
+    x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i] + add, b[4 * i + 1] + add), nb2), c2, make_float2(lb.x, lb.y));
+    x[16 + 2 * i + 1] =
+        __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2] + add, b[4 * i + 3] + add), nb2), c2, make_float2(lb.z, lb.w));
+  }
+}
+
 // Scale of the fp16 probabilities: the PV operand of block j is
 // code * w_j * kPScale / 255 (w_j = 2^(max_j - m_ref) <= 2^8), so the numerator
 // in TMEM carries a factor kPScale, removed in the epilogue.  32 keeps every
@@ -469,7 +492,12 @@ constexpr float kPScale = 32.0f;
 // rounding per probability: the code bits c from the +1.5*2^23 add are placed
 // under an fp16 exponent (2 + c/512), and one HFMA2 with the power-of-two
 // multiples 512*w and -1024*w of the fp16 weight w gives c*w.
-template <typename T, int D>
+// kRearm: the S accumulators are re-armed with the bias pattern by the
+// softmax (tcgen05.st) after each read; otherwise the first QK^T K-step
+// overwrites them and the bias bits are added in registers.  Measured: not
+// re-arming is 2% faster for non-causal D=128 launches, and 2% (causal) to 5%
+// (D=64) slower elsewhere; the host picks the instance per launch.
+template <typename T, int D, bool kRearm>
 __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t* smem, uint32_t sbase,
                                                    uint32_t tmem_base, const SoftmaxBars& bars, int nbt, int64_t q0,
                                                    int64_t bh, int split, int64_t key0, uint32_t* status,
@@ -488,7 +516,6 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
   const float qs = valid_row ? __ldg(p.qscale + bh * p.q_groups + grow / kQueryGroup) : 0.0f;
   const float c_row = qs * p.scale_log2e;
   const float* kscale = p.kscale + bh * p.k_groups + key0 / kKeyGroup;
-  const float2 nb2 = make_float2(-kBias, -kBias);
 
   // m_ref: reference max of the numerator and denominator (log2 units).  It
   // trails the true running max by less than kRescaleThreshold, which leaves
@@ -546,21 +573,13 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
       tmem_ld32_split(tm_s + buf * kKeyBlock, a);
       tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
       tmem_ld_wait();
-      // Re-arm the S buffer; s_free is signalled after the block max, by
-      // which time this store has long completed.
-      tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
-      const float c = c_row * ks;
-      const float2 c2 = make_float2(c, c);
       const uint32_t vl = sbase + S::kOffVec + s * S::kVecBytes;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 la = lds128(vl + 16 * i), lb = lds128(vl + 16 * (8 + i));
-        x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i], a[4 * i + 1]), nb2), c2, make_float2(la.x, la.y));
-        x[2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2], a[4 * i + 3]), nb2), c2, make_float2(la.z, la.w));
-        x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i], b[4 * i + 1]), nb2), c2, make_float2(lb.x, lb.y));
-        x[16 + 2 * i + 1] =
-            __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2], b[4 * i + 3]), nb2), c2, make_float2(lb.z, lb.w));
+      if constexpr (kRearm) {
+        // Re-arm the S buffer; s_free is signalled after the block max, by
+        // which time this store has long completed.
+        tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
       }
+      scores_to_x<!kRearm>(a, b, x, c_row * ks, vl);
     }
     if (p.causal) {
       // Keys after this row are masked (reference.py:86-91); only the
@@ -770,7 +789,7 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
   }
 }
 
-template <typename T, int D, bool kSage = false>
+template <typename T, int D, bool kSage = false, bool kRearm = true>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     piper_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
@@ -942,7 +961,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint64_t descK = descK0 + static_cast<uint64_t>(((jq % kStages) * S::kKBytes) >> 4);
             const uint32_t dcol = tmem_base + t * 256 + (jq & 1) * kKeyBlock;
 #pragma unroll
-            for (int kk = 0; kk < D / 32; ++kk) umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, 1u);
+            for (int kk = 0; kk < D / 32; ++kk)
+              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, (kk > 0 || kRearm) ? 1u : 0u);
             umma_commit(s_full + 8 * (t * 2 + (jq & 1)));
             qk_next[t] = jq + 1;
             progress = true;
@@ -1005,7 +1025,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, abort_flag};
-    piper_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
+    piper_softmax_role<T, D, kRearm>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
   }
 
   __syncwarp();

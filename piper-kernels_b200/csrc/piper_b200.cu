@@ -76,18 +76,22 @@ int ensure_device(int* device_out) {
   // The attention kernels redistribute registers between warpgroups with
   // setmaxnreg, which is only safe at the launch register count the split was
   // computed for.
-  const void* kernels[8] = {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, true>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, true>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>),
-                            reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>)};
-  for (int i = 0; i < 8; ++i) {
+  // Index bit 0: D=128; 2: bf16; 4: SageAttention2++; 8: Piper without S re-arm (D=128).
+  const void* kernels[10] = {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, true>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, true>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, false, false>),
+                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>)};
+  for (int i = 0; i < 10; ++i) {
     // Piper kernels (i < 4) stage 16-bit PV operands; SageAttention2++ 8-bit ones.
-    const int smem_bytes = i < 4 ? ((i % 2 == 0) ? piper::AttnSmem<64, true>::kAlloc : piper::AttnSmem<128, true>::kAlloc)
-                                 : ((i % 2 == 0) ? piper::AttnSmem<64>::kAlloc : piper::AttnSmem<128>::kAlloc);
+    const int smem_bytes = i >= 8 ? piper::AttnSmem<128, true>::kAlloc
+                           : i < 4 ? ((i % 2 == 0) ? piper::AttnSmem<64, true>::kAlloc : piper::AttnSmem<128, true>::kAlloc)
+                                   : ((i % 2 == 0) ? piper::AttnSmem<64>::kAlloc : piper::AttnSmem<128>::kAlloc);
     PIPER_CUDA(cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
     cudaFuncAttributes attr;
     PIPER_CUDA(cudaFuncGetAttributes(&attr, kernels[i]));
@@ -332,7 +336,11 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
       piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__half, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
     } else {
-      piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      if (is_causal)
+        piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      else
+        piper::piper_attention_kernel<__half, 128, false, false>
+            <<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__half, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
     }
   } else {
@@ -340,7 +348,11 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
       piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
     } else {
-      piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      if (is_causal)
+        piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      else
+        piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>
+            <<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
     }
   }
