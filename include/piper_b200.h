@@ -59,7 +59,9 @@ enum { PIPER_B200_FLOAT16 = 0, PIPER_B200_BFLOAT16 = 1 };
 
 /* Byte offsets of each intermediate inside the workspace (see layout.h in
  * the sources for shapes).  Exposed so tests can read the INT8 codes and
- * scales the prepass produced. */
+ * scales the prepass produced.  v8t holds the V codes as fp16 values (the
+ * INT8 codes exactly), transposed to [B*H, D, nk_pad]: the operand of the
+ * attention kernel's fp16 PV product. */
 typedef struct piper_b200_workspace_layout_s {
   uint64_t q8, k8, v8t, qscale, kscale, vscale, vlog2, vrcp, kmean, vmean, ksum, vsum, counter;
   uint64_t total_bytes;
@@ -101,7 +103,8 @@ int piper_b200_workspace_layout(int64_t batch, int64_t heads, int64_t query_leng
 
 /* Quantization prepass: K/V sequence means, K smoothing, per-32-row Q and
  * per-64-row K INT8 codes + scales, per-key-row V INT8 codes (centered by the
- * V mean when non-causal) + scales, into the workspace. */
+ * V mean when non-causal; stored as exact fp16 values) + scales, into the
+ * workspace. */
 int piper_b200_prepass(const void* query, const int64_t query_strides[3], const void* key,
                        const int64_t key_strides[3], const void* value,
                        const int64_t value_strides[3], int dtype, int64_t batch, int64_t heads,
