@@ -1,0 +1,71 @@
+"""Bit-level identities the attention kernels rely on, checked on the CPU.
+
+The kernels themselves are tested on the GPU against the oracle; these tests
+pin the arithmetic tricks they use, exhaustively over the codes:
+
+* the UINT8 probability code from the ``+1.5*2^23`` add, permuted under an
+  fp16 exponent, reads ``2 + c/512`` (attention.cuh, piper_softmax_role);
+* one fused multiply-add with the power-of-two multiples ``512*w`` and
+  ``-1024*w`` of the fp16 weight gives ``c*w`` rounded once to fp16, without
+  overflow over the weights the kernel can produce (attention.cuh, kPScale);
+* an INT8 V code placed, plus 128, under the fp16 exponent of 1024 and
+  reduced by 1152 is the code itself (prepass.cuh, codes_to_f16x4).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def byte_perm(x: int, y: int, selector: int) -> int:
+    """CUDA ``__byte_perm``: result byte i is byte ``(selector >> 4i) & 7`` of (y:x)."""
+    b = list(int(x).to_bytes(4, "little")) + list(int(y).to_bytes(4, "little"))
+    return int.from_bytes(bytes(b[(selector >> (4 * i)) & 7] for i in range(4)), "little")
+
+
+def f32_bits(v: float) -> int:
+    return int(np.array([v], dtype=np.float32).view(np.uint32)[0])
+
+
+def halves(word: int) -> np.ndarray:
+    return np.array([word], dtype=np.uint32).view(np.float16)
+
+
+K_BIAS = 12582912.0  # 1.5 * 2^23
+K_PSCALE = 32.0      # attention.cuh: kPScale
+
+
+def test_code_bits_read_as_fp16_two_plus_code_over_512() -> None:
+    for c0 in range(256):
+        for c1 in (0, 1, 127, 128, 254, 255, (c0 * 37) % 256):
+            y0 = f32_bits(K_BIAS + c0)
+            y1 = f32_bits(K_BIAS + c1)
+            h = halves(byte_perm(y0, y1, 0x6420))
+            assert h[0] == np.float16(2 + c0 / 512) and h[1] == np.float16(2 + c1 / 512)
+
+
+def test_weighting_is_one_rounding_of_code_times_weight() -> None:
+    # w_cur = 2^(max - m_ref) lies in (0, 2^8] (lazy rescale threshold 8).
+    exps = np.linspace(-30.0, 8.0, 761)
+    for e in exps:
+        wh = np.float16(2.0 ** e * (K_PSCALE / 255.0))
+        a = np.float16(wh * np.float16(512.0))
+        b = -np.float16(wh * np.float16(1024.0))
+        assert np.isfinite(a) and np.isfinite(b)
+        # 512 * w and 1024 * w are exact (powers of two, no overflow).
+        assert float(a) == float(wh) * 512.0 and -float(b) == float(wh) * 1024.0
+        codes = np.arange(256, dtype=np.float64)
+        h = 2.0 + codes / 512.0
+        fused = (h * float(a) + float(b)).astype(np.float16)  # exact in float64, one rounding to fp16
+        expected = (codes * float(wh)).astype(np.float16)
+        assert np.array_equal(fused, expected), e
+        assert np.isfinite(fused).all()
+
+
+def test_int8_codes_convert_to_fp16_exactly() -> None:
+    codes = np.arange(-128, 128, dtype=np.int64)
+    for c in codes:
+        u = (int(c) & 0xFF) ^ 0x80  # c + 128 as a byte
+        word = byte_perm(u | (u << 8) | (u << 16) | (u << 24), 0x64646464, 0x5140)
+        h = halves(word).astype(np.float32)
+        assert h[0] - 1152.0 == c and h[1] - 1152.0 == c
