@@ -84,3 +84,15 @@ def test_effective_tflops_formula() -> None:
     shape = {"batch_size": 1, "num_query_heads": 2, "query_length": 1000, "key_value_length": 1000, "head_dim": 128}
     assert bm.effective_tflops(shape, False, 1.0) == pytest.approx(4 * 2 * 1000 * 1000 * 128 / 1e-3 / 1e12)
     assert bm.effective_tflops(shape, True, 1.0) == pytest.approx(4 * 2 * 1000 * 1001 / 2 * 128 / 1e-3 / 1e12)
+
+
+def test_both_operators_have_record_producers() -> None:
+    assert set(bm.MEASURES) == {"piper_attention", "sage_attention_2pp"}
+    assert bm.MEASURES["piper_attention"] is bm.measure_piper_attention
+    assert bm.MEASURES["sage_attention_2pp"] is bm.measure_sage_attention_2pp
+    assert bm.PROVIDER != bm.SAGE_PROVIDER
+
+
+def test_cli_rejects_an_unknown_operator() -> None:
+    with pytest.raises(SystemExit):
+        bm.main(["--operator", "flash_attention"])
