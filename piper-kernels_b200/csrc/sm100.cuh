@@ -54,21 +54,6 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
-// One probe of the phase; the thread may be suspended in hardware for up to
-// `hint_ns` while the phase is incomplete (it wakes as soon as it completes),
-// so waiting warps do not spin on the issue slots the working warps need.
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t hint_ns = 0x100000u) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
 // Non-blocking probe of a phase (never suspends the thread).
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -257,16 +242,6 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
-      "elect.sync r|p, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
-}
-
 // ---------------------------------------------------------------- TMEM <-> registers
 // 32x32b shape: warp w of a warpgroup reads TMEM lanes 32w..32w+31, thread
 // lane i gets lane 32w+i; .xN reads N consecutive 32-bit columns.
@@ -291,21 +266,11 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
-}
 __device__ __forceinline__ void tmem_ld32_split(uint32_t taddr, uint32_t (&r)[32]) {
-#ifdef PIPER_TMEM_LD4
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tmem_ld4(taddr + 4 * i, r + 4 * i);
-#else
   tmem_ld8(taddr, r);
   tmem_ld8(taddr + 8, r + 8);
   tmem_ld8(taddr + 16, r + 16);
   tmem_ld8(taddr + 24, r + 24);
-#endif
 }
 
 __device__ __forceinline__ void tmem_ld_wait() {
@@ -328,21 +293,6 @@ __device__ __forceinline__ void tmem_st4_same(uint32_t taddr, uint32_t v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%1,%1,%1};" ::"r"(taddr), "r"(v) : "memory");
 }
 
-// Writes the same 32-bit value into 8 consecutive columns of this thread's lane.
-__device__ __forceinline__ void tmem_st8_same(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
-               : "memory");
-}
-
-// Writes the same 32-bit value into 16 consecutive columns of this thread's lane.
-__device__ __forceinline__ void tmem_st16_same(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
-
 // 16-byte shared load the compiler keeps in program order relative to the
 // other volatile asm (it will not hoist a whole block of them ahead of the
 // TMEM waits, which would pin 64 extra registers).
@@ -357,11 +307,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Exact int32 -> fp32 for |v| < 2^22: place v in the mantissa of 1.5*2^23.
-__device__ __forceinline__ float exact_i2f(uint32_t v) {
-  return __int_as_float(static_cast<int>(v + 0x4B400000u)) - 12582912.0f;
 }
 
 }  // namespace piper
