@@ -1,14 +1,16 @@
 """Benchmark of the piper_attention forward on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload c4|c2|c3|c5]
+                    [--workload c4|c2|c3|c5|c5causal]
 
 One step = one full ``piper_attention`` call (quantization prepass + fused
 attention) over one batch of seeded synthetic inputs already resident in HBM.
 The default workload is BASELINE configs[3] (c4): B1 H40 N16384 D128 bf16
-non-causal, V with a per-feature bias ~N(0,1).  Under torchrun every rank runs
-its own shard of B*H (weak scaling: 40 heads per rank, independent data, no
-collective on the data path); the reported time is the max over ranks.
+non-causal, V with a per-feature bias ~N(0,1).  Every rank generates the same
+global problem (``piper_kernels.baseline_configs``); under torchrun rank r
+computes only its contiguous slice of the flattened B*H pairs
+(``piper_attention_multi_gpu``'s partition; strong scaling of one problem,
+no collective on the data path) and the reported time is the max over ranks.
 
 ``--workload c5`` (B1 H24 N131072) splits the sequence
 over the ranks instead (strong scaling): one step is a whole
@@ -16,7 +18,7 @@ over the ranks instead (strong scaling): one step is a whole
 ring and the fp64 column totals all-reduced.
 
 Metric: TOPS = 4*B*H*Nq*Nk*D / t (the reference's formula,
-benchmarks/benchmark_attention.py:184-193), summed over ranks.
+benchmarks/benchmark_attention.py:184-193) for the whole job.
 """
 
 from __future__ import annotations
@@ -38,71 +40,26 @@ for _p in (REPO / "piper-kernels_b200", REPO):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-WORKLOADS = {
-    # name: (B, H, N, D, dtype, causal, description)
-    "c4": (1, 40, 16384, 128, torch.bfloat16, False,
-           "piper_attention non-causal B1 H40 N16384 D128 bf16 (BASELINE configs[3]); V bias ~N(0,1)"),
-    "c2": (2, 24, 4096, 128, torch.bfloat16, False,
-           "piper_attention non-causal B2 H24 N4096 D128 bf16 (BASELINE configs[1]); 4 K outlier channels +8, V bias ~N(0,2)"),
-    "c3": (4, 32, 8192, 128, torch.float16, True,
-           "piper_attention causal B4 H32 N8192 D128 fp16 (BASELINE configs[2]); K offset ~N(0,2)"),
-    "c5": (1, 24, 131072, 128, torch.bfloat16, False,
-           "piper_attention non-causal sequence-sharded ring B1 H24 N131072 D128 bf16 (BASELINE configs[4]); "
-           "V bias ~N(0,1)"),
-    "c5causal": (1, 24, 131072, 128, torch.bfloat16, True,
-                 "piper_attention CAUSAL sequence-sharded ring, zig-zag shards, B1 H24 N131072 D128 bf16 "
-                 "(the c5 shape with the causal mask; not a BASELINE config)"),
-}
+from piper_kernels.baseline_configs import CONFIGS, make_inputs  # noqa: E402
+
 # Workloads whose sequence is split over the ranks (strong scaling, NCCL ring).
 RING_WORKLOADS = {"c5", "c5causal"}
+BENCH_WORKLOADS = ("c2", "c3", "c4", "c5", "c5causal")
 METRIC = "piper_attention TOPS (4*B*H*N^2*D/t) at D=128"
 INT8_NOMINAL_TOPS = 4500.0
+# Parity bounds of the reference's own GPU tests against its portable path
+# (tests/attention/piper_attention/test_triton.py:139-145), plus a cosine floor.
+PARITY_MEAN_ABS = 0.003
+PARITY_MAX_ABS = 0.12
+PARITY_COSINE = 0.9999
+# The CPU sample of the c5 workloads: this many query rows of one head
+# against all keys (one whole head is about a minute of CPU work).
+RING_SAMPLE_ROWS = 2048
 
 
-def make_inputs(name: str, rank: int, device: torch.device):
-    """Seeded synthetic Q/K/V with the BASELINE distributions (one rank's shard)."""
-    b, h, n, d, dtype, causal, _ = WORKLOADS[name]
-    g = torch.Generator(device=device).manual_seed(1000 + rank)
-    shape = (b, h, n, d)
-    q = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
-    k = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
-    v = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
-    if name == "c2":
-        channels = torch.randperm(d, generator=g, device=device)[:4]
-        k[..., channels] += 8.0
-        v += torch.randn((b, h, 1, d), generator=g, device=device) * 2.0
-    elif name == "c3":
-        k += torch.randn((b, h, 1, d), generator=g, device=device) * 2.0
-    else:
-        v += torch.randn((b, h, 1, d), generator=g, device=device)
-    return q.to(dtype), k.to(dtype), v.to(dtype), causal
-
-
-def make_ring_inputs(name: str, rank: int, world: int, device: torch.device, heads: int | None = None):
-    """This rank's rows of the seeded full sequence (identical on every rank).
-
-    The union over ranks is the same tensor for every world size, so the
-    ring's output rows equal one GPU's (strong scaling).  Causal workloads use
-    the zig-zag layout (chunks r and 2*world-1-r), the others contiguous rows.
-    """
-    from piper_kernels.attention.piper_attention.ring import zigzag_shard
-
-    b, h, n, d, dtype, causal, _ = WORKLOADS[name]
-    h = h if heads is None else heads
-    g = torch.Generator(device=device).manual_seed(1000)
-    shard = n // world
-
-    def mine(t):
-        if causal:
-            return zigzag_shard(t, rank, world)
-        return t[:, :, rank * shard : (rank + 1) * shard]
-
-    shape = (b, h, n, d)
-    q = mine(torch.randn(shape, generator=g, device=device)).to(dtype).contiguous()
-    k = mine(torch.randn(shape, generator=g, device=device)).to(dtype).contiguous()
-    v = mine(torch.randn(shape, generator=g, device=device))
-    v = (v + torch.randn((b, h, 1, d), generator=g, device=device)).to(dtype).contiguous()
-    return q, k, v
+def workload(name: str):
+    cfg = CONFIGS[name]
+    return cfg.batch, cfg.heads, cfg.seq_len, cfg.head_dim, cfg.dtype, cfg.is_causal, cfg.description
 
 
 def attention_ops(b: int, h: int, nq: int, nk: int, d: int) -> float:
@@ -171,78 +128,133 @@ def profiled_traffic(workload: str):
     return None
 
 
-def cpu_baseline(workload: str, steps: int = 1) -> dict:
-    """The oracle (a C port of the reference's portable path) on one head of the workload.
+def oracle_sample(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, rows: int,
+                  runs: int = 1) -> dict:
+    """The oracle (a C port of the reference's portable path) on one head, timed.
 
-    Heads are independent in the reference, so the sample is one (b,h) slice
-    of the seeded inputs at the full sequence length; TOPS scale linearly.
+    ``q``/``k``/``v`` are one head, ``[1, 1, N, D]`` on any device: the GPU
+    arm's own tensors.  The first ``rows`` query rows attend to all keys
+    (query rows are independent, so TOPS scale with them; the prepass of all
+    keys is inside the timed region).  Returns the timing, the fp32 output
+    rows and the oracle's prepass for parity checks.
     """
     from oracle import oracle
 
-    b, h, n, d, dtype, causal, _ = WORKLOADS[workload]
+    n, d = k.shape[2], k.shape[3]
     cores = os.cpu_count() or 1
     oracle.build()
     oracle.set_threads(cores)
-    if workload in RING_WORKLOADS:
-        q, k, v = make_ring_inputs(workload, 0, 1, torch.device("cpu"), heads=1)
-    else:
-        q, k, v, _ = make_inputs(workload, 0, torch.device("cpu"))
-        q, k, v = q[:1, :1], k[:1, :1], v[:1, :1]
-    # At N=131072 one head is still ~70 s of CPU work: time the first
-    # `rows` queries against the whole sequence (queries are independent, so
-    # TOPS scale with the rows; the prepass of all keys is included).
-    rows = n if n <= 16384 else 8192
-    times = []
-    for _ in range(max(1, steps)):
+    qc, kc, vc = (t.detach().cpu() for t in (q, k, v))
+    times, out, prepared = [], None, None
+    for _ in range(max(1, runs)):
         t0 = time.perf_counter()
-        prepared = oracle.prepare(q, k, v, causal)
-        if rows < n:
-            prepared.query_int8 = np.ascontiguousarray(prepared.query_int8[:, :, :rows])
-            prepared.query_scale = np.ascontiguousarray(prepared.query_scale[:, :, : rows // 32])
-        oracle.attention_prepared(prepared, d**-0.5, causal)
+        prepared = oracle.prepare(qc[:, :, :rows], kc, vc, causal)
+        out = oracle.attention_prepared(prepared, d**-0.5, causal)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    ops = attention_ops(1, 1, rows, n, d)
     what = "full sequence" if rows == n else f"first {rows} query rows x all {n} keys"
     return {
-        "value": ops / t / 1e12,
-        "unit": "TOPS",
+        "tops": attention_ops(1, 1, rows, n, d) / t / 1e12,  # the metric's formula (full N^2 when causal)
+        "seconds": t,
+        "runs": len(times),
         "cores": cores,
-        "kind": "port",
-        "sample": f"1 of {b * h} heads (B1 H1 N{n} D{d}), {what}; {len(times)} run(s), median {t:.2f} s",
-        "seconds_per_sample": t * (n / rows),
+        "what": what,
+        "out": out,
+        "prepared": prepared,
     }
+
+
+def parity_against_oracle(sample: dict, out_gpu: torch.Tensor, prepared_gpu, rows: int) -> dict:
+    """GPU output and codes of head 0 against the oracle on the same tensors."""
+    ref = torch.from_numpy(sample["out"]).to(out_gpu.dtype).double()
+    mine = out_gpu[:, :1, :rows].detach().cpu().double()
+    err = (mine - ref).abs()
+    cos = torch.nn.functional.cosine_similarity(mine.flatten(), ref.flatten(), dim=0).item()
+    p = sample["prepared"]
+    n = p.key_int8.shape[2]
+    codes = {
+        "query_int8": bool(np.array_equal(prepared_gpu.query_int8[:, :1, :rows].cpu().numpy(), p.query_int8)),
+        "query_scale": bool(np.array_equal(prepared_gpu.query_scale[:, :1, : (rows + 31) // 32].cpu().numpy(),
+                                           p.query_scale)),
+        "key_int8": bool(np.array_equal(prepared_gpu.key_int8[:, :1].cpu().numpy(), p.key_int8)),
+        "key_scale": bool(np.array_equal(prepared_gpu.key_scale[:, :1].cpu().numpy(), p.key_scale)),
+        "value_int8": bool(np.array_equal(prepared_gpu.value_int8[:, :1].cpu().numpy(), p.value_int8)),
+        "value_scale": bool(np.array_equal(prepared_gpu.value_scale[:, :1, :n].cpu().numpy(), p.value_scale)),
+    }
+    result = {
+        "sample": f"head (b=0, h=0) of the timed inputs, {sample['what']}; oracle on the same tensors",
+        "max_abs": err.max().item(),
+        "mean_abs": err.mean().item(),
+        "cosine": cos,
+        "codes_equal": all(codes.values()),
+        "codes": codes,
+        "bounds": {"max_abs": PARITY_MAX_ABS, "mean_abs": PARITY_MEAN_ABS, "cosine": PARITY_COSINE},
+    }
+    result["pass"] = bool(result["codes_equal"] and result["max_abs"] < PARITY_MAX_ABS
+                          and result["mean_abs"] < PARITY_MEAN_ABS and cos > PARITY_COSINE)
+    return result
 
 
 def run_reference(args) -> None:
+    """The reference arm: the oracle port on the host cores, on the same inputs as the GPU arm.
+
+    One sample = one head of the workload (for c5, its first 2048 query rows
+    against all keys), timed whole; ``steps`` counts the samples run and
+    ``ms_per_step`` is one sample's time.  The rate scales linearly to the
+    whole job (heads and query rows are independent), reported separately.
+    """
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    b, h, n, d, dtype, causal, desc = WORKLOADS[args.workload]
-    base = cpu_baseline(args.workload, steps=max(1, min(args.steps, 2)))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
+    b, h, n, d, dtype, causal, desc = workload(args.workload)
     ring = args.workload in RING_WORKLOADS
-    units = b * h * (1 if ring else world)  # ring: the whole sequence is the job
+    gen_device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))) if torch.cuda.is_available() else None
+    q, k, v = make_inputs(args.workload, gen_device or "cpu")
+    q, k, v = (t[:1, :1].cpu() for t in (q, k, v))
+    rows = RING_SAMPLE_ROWS if ring else n
+    samples = max(1, min(args.steps, 2))
+    s = oracle_sample(q, k, v, causal, rows, runs=samples)
+    full_ops = attention_ops(b, h, n, n, d)
+    sample_ops = attention_ops(1, 1, rows, n, d)
     line = {
         "impl": "reference",
         "metric": METRIC,
-        "value": base["value"],
+        "value": s["tops"],
         "unit": "TOPS",
         "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": base["seconds_per_sample"] * units * 1e3,
+        "steps": s["runs"],
+        "warmup": 0,
+        "requested_steps": args.steps,
+        "requested_warmup": args.warmup,
+        "ms_per_step": s["seconds"] * 1e3,
+        "step": "one sample: " + s["what"] + " of one head",
+        "extrapolated_ms_per_job": s["seconds"] * full_ops / sample_ops * 1e3,
         "higher_is_better": True,
-        "scaling": "strong" if ring else "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8",
-        "data": "synthetic (seeded randn with the BASELINE distributions)",
-        "config": {"workload": desc, "global_batch": b if ring else b * world, "heads": h, "seq_len": n,
-                   "head_dim": d},
-        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
-        "e2e": {"value": base["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "data": "synthetic (seeded randn with the BASELINE distributions; the GPU arm's own tensors)"
+                if gen_device is not None else "synthetic (seeded randn with the BASELINE distributions)",
+        "config": {"workload": desc, "global_batch": b, "heads": h, "seq_len": n, "head_dim": d},
+        "cpu_baseline": {
+            "value": s["tops"], "unit": "TOPS", "cores": s["cores"], "kind": "port",
+            "value_per_core": s["tops"] / s["cores"],
+            "sample": f"1 of {b * h} heads (B1 H1 N{n} D{d}), {s['what']}; {s['runs']} run(s), "
+                      f"median {s['seconds']:.2f} s",
+        },
+        "e2e": {"value": s["tops"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _plan_kernels(b: int, h: int, nq: int, nk: int, d: int, causal: bool) -> int:
+    """Kernels one prepared attention call launches (the attention kernel, plus the split merge)."""
+    from piper_kernels._targets import AcceleratorTarget
+    from piper_kernels.attention.piper_attention._policy import select_execution_plan
+
+    target = AcceleratorTarget.from_device(torch.device("cuda", torch.cuda.current_device()))
+    return select_execution_plan(target, batch=b, heads=h, query_length=nq, key_length=nk, head_dim=d,
+                                 is_causal=causal).kernels
 
 
 def run_b200(args) -> None:
@@ -254,6 +266,7 @@ def run_b200(args) -> None:
         prepare_piper_attention,
         run_piper_attention_host,
     )
+    from piper_kernels.attention.piper_attention.multi_gpu import head_partition, local_heads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -264,11 +277,17 @@ def run_b200(args) -> None:
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    b, h, n, d, dtype, causal, desc = WORKLOADS[args.workload]
-    q, k, v, causal = make_inputs(args.workload, rank, dev)
+    b, h, n, d, dtype, causal, desc = workload(args.workload)
+    # The global problem, identical on every rank; this rank keeps its B*H slice.
+    q_all, k_all, v_all = make_inputs(args.workload, dev)
+    q, k, v = (local_heads(t, rank, world).contiguous() for t in (q_all, k_all, v_all))
+    del q_all, k_all, v_all
+    units = q.shape[1]
+    first_unit = head_partition(b * h, world)[rank][0]
     scale = d**-0.5
-    ops_rank = attention_ops(b, h, n, n, d) * (0.5 * (n + 1) / n if causal else 1.0)
-    ops_full = attention_ops(b, h, n, n, d)
+    causal_factor = 0.5 * (n + 1) / n if causal else 1.0
+    ops_rank = attention_ops(1, units, n, n, d) * causal_factor
+    ops_job = attention_ops(b, h, n, n, d)  # the reference's formula (full N^2 even when causal)
 
     def barrier():
         if world > 1:
@@ -283,11 +302,13 @@ def run_b200(args) -> None:
         return float(t.item())
 
     stream = torch.cuda.current_stream(dev)
-    ws_bytes = int(_native.workspace_layout(b, h, n, n, d).total_bytes)
+    ws_bytes = int(_native.workspace_layout(1, units, n, n, d).total_bytes)
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     out = torch.empty_like(q)
+    prepared = None
 
     def step(events=None):
+        nonlocal prepared
         if events is not None:
             events[0].record(stream)
         prepared = prepare_piper_attention(q, k, v, causal, workspace=workspace)
@@ -322,9 +343,10 @@ def run_b200(args) -> None:
         if status != 0:
             raise RuntimeError(f"a kernel reported a timed-out wait (status {status:#x})")
 
-        # End to end with host buffers: pinned Q/K/V in, pinned output out,
-        # through the library's host-to-host entry point (chunks of heads
-        # stream through the GPU with the copies overlapping the kernels).
+        # End to end with host buffers: this rank's pinned Q/K/V slice in, its
+        # pinned output slice out, through the library's host-to-host entry
+        # point (chunks of heads stream through the GPU with the copies
+        # overlapping the kernels).
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
         e2e_steps = max(2, min(args.steps, 5))
@@ -367,17 +389,24 @@ def run_b200(args) -> None:
         serial_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
 
     ms_per_step = elapsed_ms / args.steps
-    value = ops_full * world / (ms_per_step * 1e-3) / 1e12
+    value = ops_job / (ms_per_step * 1e-3) / 1e12
     measured = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
     bf16_peak = measured.get("bf16_tflops")
     int8_peak = 2.0 * bf16_peak if bf16_peak else 2.0 * 1590.0
     peak_note = "2 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json)" if bf16_peak else "2 x fallback 1.59 PF bf16"
     attn_tops = ops_rank / (attn_avg_ms * 1e-3) / 1e12
     hbm = measured.get("hbm_gbs") or 6650.0
-    # Read Q, K, V once (2 B each); write INT8 Q and K codes and the fp16 V codes
-    # (1 + 1 + 2 B); plus the scales and per-key vectors.
-    prepass_bytes = b * h * n * d * (3 * 2 + 4) + b * h * (n // 32 + n // 64 + 3 * n) * 4
+    # Compulsory bytes of the prepass for this rank's slice: read Q, K, V once
+    # (2 B each); write INT8 Q and K codes and the V codes (stored as fp16,
+    # 2 B); plus the per-group scales and the three per-key vectors.
+    elems = units * n * d
+    prepass_bytes = elems * (3 * 2 + 1 + 1 + 2) + units * (n // 32 + n // 64 + 3 * n) * 4
+    prepass_bytes_int8_v = prepass_bytes - elems  # the same with INT8 V codes (1 B), the survey's count
+    launches = (2 + _plan_kernels(1, units, n, n, d, causal)) * args.steps
     if rank == 0:
+        parallelism = ("one GPU" if world == 1 else
+                       f"B*H split x{world}: rank r runs a contiguous slice of the {b * h} (b,h) pairs "
+                       f"({units} on rank 0), no data-path collective")
         line = {
             "metric": METRIC,
             "value": value,
@@ -387,19 +416,20 @@ def run_b200(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": ms_per_step,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "int8",
             "data": "synthetic (seeded randn with the BASELINE distributions; inputs resident in HBM)",
             "config": {
                 "workload": desc,
-                "global_batch": b * world,
+                "global_batch": b,
                 "heads": h,
                 "seq_len": n,
                 "head_dim": d,
                 "causal": causal,
-                "parallelism": f"heads sharded x{world}, no data-path collective",
-                "l2": "inputs larger than L2 (Q/K/V of one step = %.0f MB)" % (3 * b * h * n * d * 2 / 1e6),
+                "parallelism": parallelism,
+                "units_rank0": units,
+                "l2": "inputs larger than L2 (Q/K/V of one rank's step = %.0f MB)" % (3 * elems * 2 / 1e6),
             },
             "roofline": {
                 "bound": "tensor",
@@ -412,7 +442,7 @@ def run_b200(args) -> None:
                 "kernel": "piper_attention_kernel",
                 "ms_per_launch": attn_avg_ms,
                 "ops_per_launch": ops_rank,
-                "traffic": profiled_traffic(args.workload),
+                "traffic": profiled_traffic(args.workload) if world == 1 else None,
             },
             "prepass": {
                 "ms_per_call": prepass_avg_ms,
@@ -420,22 +450,33 @@ def run_b200(args) -> None:
                 "achieved_gbs": prepass_bytes / (prepass_avg_ms * 1e-3) / 1e9,
                 "peak_gbs": hbm,
                 "frac": prepass_bytes / (prepass_avg_ms * 1e-3) / 1e9 / hbm,
+                "frac_int8_v_bytes": prepass_bytes_int8_v / (prepass_avg_ms * 1e-3) / 1e9 / hbm,
             },
-            "kernel_only_tops": ops_full * world / (attn_avg_ms * 1e-3) / 1e12,
+            "kernel_only_tops": ops_job / (attn_avg_ms * 1e-3) / 1e12,
             "e2e": {
-                "value": ops_full * world / (e2e_ms * 1e-3) / 1e12,
+                "value": ops_job / (e2e_ms * 1e-3) / 1e12,
                 "unit": "TOPS",
                 "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
-                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "h2d_bytes_per_step": 3 * q.numel() * q.element_size() * world,
+                "d2h_bytes_per_step": out.numel() * out.element_size() * world,
                 "api": "piper_b200_attention_fwd_host (pinned host buffers, copies overlapped with kernels)",
-                "serial_copies_tops": ops_full * world / (serial_ms * 1e-3) / 1e12,
+                "serial_copies_tops": ops_job / (serial_ms * 1e-3) / 1e12,
             },
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
-        if not args.skip_cpu_baseline:
-            line["cpu_baseline"] = {kk: vv for kk, vv in cpu_baseline(args.workload).items() if kk != "seconds_per_sample"}
+        if first_unit == 0 and not args.skip_cpu_baseline:
+            # Head (0, 0) of the global problem is rank 0's first pair: the
+            # oracle runs on those very tensors, timed (the CPU baseline, at
+            # one GPU) and compared with the GPU's output and codes (parity).
+            sample = oracle_sample(q[:, :1], k[:, :1], v[:, :1], causal, n)
+            line["parity"] = parity_against_oracle(sample, out, prepared, n)
+            if world == 1:
+                line["cpu_baseline"] = {
+                    "value": sample["tops"], "unit": "TOPS", "cores": sample["cores"], "kind": "port",
+                    "sample": f"head (0,0) of the timed inputs (B1 H1 N{n} D{d}), {sample['what']}; "
+                              f"{sample['seconds']:.2f} s",
+                }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -465,12 +506,21 @@ def run_ring(args) -> None:
         options = dist.ProcessGroupNCCL.Options()
         options.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev, pg_options=options)
-    b, h, n, d, dtype, causal, desc = WORKLOADS[args.workload]
+    from piper_kernels.attention.piper_attention.ring import zigzag_shard
+
+    b, h, n, d, dtype, causal, desc = workload(args.workload)
     layout = "zigzag" if causal else "contiguous"
     if n % ((128 if causal else 64) * world):
         raise SystemExit(f"N={n} does not split into {world} shards of whole 64-row groups")
     shard = n // world
-    q, k, v = make_ring_inputs(args.workload, rank, world, dev)
+    # The global sequence, identical on every rank; this rank keeps its rows
+    # (chunks r and 2*world-1-r of 2*world for the zig-zag layout).
+    q_all, k_all, v_all = make_inputs(args.workload, dev)
+    if causal:
+        q, k, v = (zigzag_shard(t, rank, world).contiguous() for t in (q_all, k_all, v_all))
+    else:
+        q, k, v = (t[:, :, rank * shard : (rank + 1) * shard].contiguous() for t in (q_all, k_all, v_all))
+    del q_all, k_all, v_all
     scale = d**-0.5
     stream = torch.cuda.current_stream(dev)
 
@@ -498,7 +548,7 @@ def run_ring(args) -> None:
         with ClockSampler(local) as clocks:
             start.record(stream)
             for _ in range(args.steps):
-                ring_piper_attention(q, k, v, is_causal=causal, layout=layout)
+                out_last = ring_piper_attention(q, k, v, is_causal=causal, layout=layout)
             stop.record(stream)
             torch.cuda.synchronize(dev)
         elapsed_ms = max_over_ranks(start.elapsed_time(stop))
@@ -528,7 +578,17 @@ def run_ring(args) -> None:
         k1.record(stream)
         torch.cuda.synchronize(dev)
         attn_ms = max_over_ranks(k0.elapsed_time(k1) / launches)
-        del prepared, state
+        del state
+        parity = None
+        sample = None
+        if world == 1 and not args.skip_cpu_baseline:
+            # One GPU holds the whole sequence: the oracle runs on head (0,0)
+            # of the timed tensors (its first rows against all keys), timed
+            # (the CPU baseline) and compared with the timed output and the
+            # prepass codes of the same head (parity).
+            sample = oracle_sample(q[:, :1], k[:, :1], v[:, :1], causal, RING_SAMPLE_ROWS)
+            parity = parity_against_oracle(sample, out_last, prepared, RING_SAMPLE_ROWS)
+        del prepared, out_last
 
         # End to end with host buffers: this rank's pinned Q/K/V rows in, its
         # output rows out, the ring in between.
@@ -624,8 +684,13 @@ def run_ring(args) -> None:
             "gpu_launches": (3 + launches_per_step) * args.steps,
             "clocks": clocks.summary(),
         }
-        if not args.skip_cpu_baseline and not causal:
-            line["cpu_baseline"] = {kk: vv for kk, vv in cpu_baseline(args.workload).items() if kk != "seconds_per_sample"}
+        if parity is not None:
+            line["parity"] = parity
+            line["cpu_baseline"] = {
+                "value": sample["tops"], "unit": "TOPS", "cores": sample["cores"], "kind": "port",
+                "sample": f"head (0,0) of the timed inputs (B1 H1 N{n} D{d}), {sample['what']}; "
+                          f"{sample['seconds']:.2f} s",
+            }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -638,7 +703,7 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
+    parser.add_argument("--workload", choices=BENCH_WORKLOADS, default="c4")
     parser.add_argument("--skip-cpu-baseline", action="store_true")
     args = parser.parse_args()
     if args.warmup < 3:

@@ -125,6 +125,50 @@ int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], 
                              int64_t head_dim, double scale, int is_causal, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* ---- Execution plan ----------------------------------------------------
+ * Host-side launch choices of one attention call, the counterpart of the
+ * reference's PiperAttentionExecutionPlan / select_execution_plan
+ * (src/piper_kernels/attention/piper_attention/_policy.py:14-96) and of its
+ * offline tuner's candidate plans (benchmarks/tune_piper_attention.py:53-101).
+ * The first three fields are fixed by the compiled kernels and only
+ * reported; the others are run-time choices. */
+typedef struct piper_b200_plan_s {
+  int32_t tile_rows;   /* query rows per CTA (two 128-row tiles) */
+  int32_t key_block;   /* keys per online-softmax block */
+  int32_t stages;      /* depth of the kernel's K/V shared-memory ring */
+  int32_t rearm;       /* 1: the S accumulators are re-armed with the bias pattern after each read;
+                          0: the first QK^T step overwrites them and the bias is added in registers
+                          (an instance that exists for D=128 only) */
+  int32_t heavy_first; /* causal: query tiles with the most visible keys are scheduled first */
+  int32_t split_k;     /* key ranges per tile of the split-KV tail; 0 = no split */
+  int64_t tiles;       /* query tiles of the launch: B*H*ceil(Nq / tile_rows) */
+  int64_t tail_tiles;  /* trailing tiles cut into split_k key ranges (0 when split_k is 0) */
+  int64_t ctas;        /* CTAs of the attention kernel: tiles - tail_tiles + tail_tiles*split_k */
+  int32_t kernels;     /* kernel launches of one prepared call: 1, or 2 with the split merge */
+  int32_t sms;         /* SM count the plan was made for */
+} piper_b200_plan_t;
+
+/* The production plan for a problem on a device with `sms` SMs (0 = the
+ * current device's count, or 148 when no device is visible).  `split_region`
+ * says whether the workspace includes the optional split-KV region (a
+ * workspace of piper_b200_workspace_bytes bytes does).  Pure host logic: it
+ * needs no GPU. */
+int piper_b200_select_plan(int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                           int64_t head_dim, int is_causal, int sms, int split_region,
+                           piper_b200_plan_t* plan);
+
+/* piper_b200_attention_prepared with an explicit plan (from
+ * piper_b200_select_plan, possibly edited: rearm, heavy_first, split_k and
+ * tail_tiles are honoured; tiles, ctas and kernels are recomputed).  Plans
+ * that the kernels cannot run (a split for causal attention, rearm 0 at D=64,
+ * more split CTAs than the workspace's split region holds) are rejected with
+ * PIPER_B200_ERR_INVALID_ARGUMENT. */
+int piper_b200_attention_prepared_plan(void* out, int dtype, int64_t batch, int64_t heads,
+                                       int64_t query_length, int64_t key_length, int64_t head_dim,
+                                       double scale, int is_causal, const void* workspace,
+                                       size_t workspace_bytes, const piper_b200_plan_t* plan,
+                                       void* stream);
+
 /* ---- Sequence-sharded (ring) attention --------------------------------
  * For a sequence split over ranks (rank r holds query/key/value rows of
  * shard r).  No counterpart in the reference, which runs on one GPU; these
@@ -258,13 +302,19 @@ int piper_b200_sage2pp_fwd(const void* query, const int64_t query_strides[3], co
  * The caller still passes inputs and output.  The scratch comes from a
  * fixed 16 MiB array (PIPER_B200_NO_ALLOC_WORKSPACE_BYTES) compiled into this
  * library: every GPU that loads the library holds that array until the
- * process exits.  A problem whose workspace (piper_b200_workspace_bytes)
- * exceeds it is rejected with PIPER_B200_ERR_WORKSPACE_TOO_SMALL; no cudaMalloc,
- * cudaFree or other allocating call is made.  The first call on a device looks
- * up the array's device address for that device (make that first call before
- * any stream capture).  All calls on a device share the one array, so two
- * calls whose work overlaps on the GPU (different streams, no ordering
- * between them) race and corrupt each other; order such calls on one stream. */
+ * process exits.  The limit applies to the required part of the workspace,
+ * the bytes before its optional split-KV region (the `split_state` offset of
+ * piper_b200_workspace_layout): a problem whose required part exceeds 16 MiB
+ * is rejected with PIPER_B200_ERR_WORKSPACE_TOO_SMALL.  When the whole
+ * workspace (piper_b200_workspace_bytes, split region included) does not fit
+ * but its required part does, the call runs without the split-KV tail (the
+ * same output to fp32 rounding).  No cudaMalloc, cudaFree or other allocating
+ * call is made.  The first call on a device (and the first after the device's
+ * context is reset) looks up the array's device address for that context
+ * (make that first call before any stream capture).  All calls on a device
+ * share the one array, so two calls whose work overlaps on the GPU (different
+ * streams, no ordering between them) race and corrupt each other; order such
+ * calls on one stream. */
 int piper_b200_attention_fwd_no_alloc(const void* query, const int64_t query_strides[3],
                                       const void* key, const int64_t key_strides[3],
                                       const void* value, const int64_t value_strides[3], void* out,

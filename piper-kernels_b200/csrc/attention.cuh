@@ -109,6 +109,7 @@ struct AttnParams {
   int64_t heads, nq, nk, nk_pad, q_groups, k_groups;
   float scale_log2e;
   int causal;
+  int reverse_tiles;  // schedule query tiles last-first (causal: heaviest first)
   int q_tiles;  // ceil(Nq / 256)
   uint64_t wait_budget_ns;
   // Sequence shards.  Causal visibility is key <= query + causal_shift in
@@ -821,8 +822,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int split = wu.split;  // >= 0: this CTA is key range `split` of a tail tile
   const int64_t bh = wu.tile / p.q_tiles;
   const int qtl = static_cast<int>(wu.tile % p.q_tiles);
-  // Causal work grows with the query position: hand out heavy tiles first.
-  const int qt = p.causal ? (p.q_tiles - 1 - qtl) : qtl;
+  // Causal work grows with the query position: the plan hands out heavy tiles first.
+  const int qt = p.reverse_tiles ? (p.q_tiles - 1 - qtl) : qtl;
   const int64_t q0 = static_cast<int64_t>(qt) * kTileM * kTiles;
   int64_t key0 = p.k_key0;  // first key of this CTA's range
   int64_t nk_cta = p.nk;
@@ -1048,7 +1049,8 @@ __global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const Attn
   const int64_t st = blockIdx.x;
   const int64_t tile = p.main_units + st;
   const int64_t bh = tile / p.q_tiles;
-  const int64_t row = (tile % p.q_tiles) * (kTileM * kTiles) + threadIdx.x;
+  const int64_t qtl = tile % p.q_tiles;  // same tile order as the attention kernel
+  const int64_t row = (p.reverse_tiles ? (p.q_tiles - 1 - qtl) : qtl) * (kTileM * kTiles) + threadIdx.x;
   if (row >= p.nq) return;
   constexpr int kRows = kTileM * kTiles;
   const float2* ml = reinterpret_cast<const float2*>(p.split_state + p.split_units * kRows * D);

@@ -43,21 +43,59 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
 constexpr int kMaxDevices = 64;
 std::mutex g_init_mutex;
 bool g_device_ready[kMaxDevices] = {};
+unsigned long long g_device_context[kMaxDevices] = {};  // context the set-up was done in
 int g_device_sms[kMaxDevices] = {};
 EncodeTiledFn g_encode = nullptr;
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
 
-// One-time per-device set-up (thread safe): architecture check and the
-// dynamic shared-memory opt-in of the attention kernels.
+// Identity of the calling thread's current CUDA context (0 when none is
+// current).  Per-device set-up lives in a context: after cudaDeviceReset, or
+// once the primary context is destroyed and made again, kernel attributes and
+// symbol addresses of the old context no longer apply, and the new context
+// has a new id (cuCtxGetId ids are unique for the life of the process).
+// Called with g_init_mutex held.
+unsigned long long current_context_id() {
+  if (g_ctx_get_current == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(fn);
+    cudaGetLastError();
+  }
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current == nullptr || g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (g_ctx_get_id != nullptr && g_ctx_get_id(ctx, &id) == CUDA_SUCCESS) return id + 1;
+  return static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(ctx));
+}
+
+// Per-device set-up (thread safe), redone whenever the device's context
+// changes: architecture check and the dynamic shared-memory opt-in of the
+// attention kernels.
 int ensure_device(int* device_out) {
   int device = 0;
   PIPER_CUDA(cudaGetDevice(&device));
   if (device < 0 || device >= kMaxDevices) return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE, "device index out of range");
   *device_out = device;
+  // Makes the device's primary context current (creating it after a reset),
+  // so that its id can be compared with the one the set-up was done in.
+  PIPER_CUDA(cudaSetDevice(device));
   std::lock_guard<std::mutex> lock(g_init_mutex);
-  if (g_device_ready[device]) return PIPER_B200_OK;
+  const unsigned long long context = current_context_id();
+  if (g_device_ready[device] && context != 0 && g_device_context[device] == context) return PIPER_B200_OK;
+  g_device_ready[device] = false;
   cudaDeviceProp prop;
   PIPER_CUDA(cudaGetDeviceProperties(&prop, device));
   g_device_sms[device] = prop.multiProcessorCount;
@@ -105,6 +143,7 @@ int ensure_device(int* device_out) {
       return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE, "an attention CTA does not fit on one SM of this device");
   }
   g_device_ready[device] = true;
+  g_device_context[device] = current_context_id();
   return PIPER_B200_OK;
 }
 
@@ -232,6 +271,78 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
   return PIPER_B200_OK;
 }
 
+// Production plan of one attention launch over `q_rows` query rows and `keys`
+// keys per head (pure host logic).  The tile shape and ring depth are fixed by
+// the compiled kernels; the rest are the measured choices:
+//   - rearm: the instance that re-arms the S accumulators with the bias
+//     pattern is 2-5% faster for causal and D=64 launches; for non-causal
+//     D=128 the instance that adds the bias in registers is 2% faster.
+//   - heavy_first: causal tiles with more visible keys start first.
+//   - split-KV tail: when the tiles do not fill whole waves on the SMs, the
+//     `tail` tiles of the last partial wave are cut into
+//     k = min(kMaxSplits, SMs / tail, key blocks / 2) key ranges, so that the
+//     last wave ends sooner (non-causal launches, and only when the workspace
+//     has the split region).
+piper_b200_plan_t make_plan(int64_t bh, int64_t q_rows, int64_t keys, int64_t d, bool causal, int sms,
+                            bool split_region, int64_t split_units_max) {
+  piper_b200_plan_t P{};
+  P.tile_rows = piper::kTileM * piper::kTiles;
+  P.key_block = piper::kKeyBlock;
+  P.stages = d == 128 ? piper::AttnSmem<128, true>::kStages : piper::AttnSmem<64, true>::kStages;
+  P.rearm = (d == 128 && !causal) ? 0 : 1;
+  P.heavy_first = causal ? 1 : 0;
+  P.sms = sms;
+  P.tiles = (q_rows + P.tile_rows - 1) / P.tile_rows * bh;
+  if (!causal && split_region && P.tiles < (int64_t(1) << 30)) {
+    const int64_t tail = P.tiles % sms;
+    const int64_t blocks = (keys + piper::kKeyBlock - 1) / piper::kKeyBlock;
+    const int64_t k = tail > 0 ? std::min<int64_t>({int64_t(piper::kMaxSplits), sms / tail, blocks / 2}) : 0;
+    if (k >= 2 && tail * k <= split_units_max) {
+      P.split_k = static_cast<int32_t>(k);
+      P.tail_tiles = tail;
+    }
+  }
+  P.ctas = P.tiles - P.tail_tiles + P.tail_tiles * P.split_k;
+  P.kernels = P.split_k > 0 ? 2 : 1;
+  return P;
+}
+
+// Checks a caller-edited plan against what the kernels can run and fills in
+// its derived fields.
+int check_plan(piper_b200_plan_t* P, int64_t bh, int64_t q_rows, int64_t keys, int64_t d, bool causal,
+               bool split_region, int64_t split_units_max) {
+  const piper_b200_plan_t ref = make_plan(bh, q_rows, keys, d, causal, P->sms > 0 ? P->sms : 148, false, 0);
+  if (P->tile_rows != ref.tile_rows || P->key_block != ref.key_block || P->stages != ref.stages)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan tile_rows, key_block and stages are fixed by the kernels (" +
+                                                     std::to_string(ref.tile_rows) + ", " +
+                                                     std::to_string(ref.key_block) + ", " +
+                                                     std::to_string(ref.stages) + ")");
+  if ((P->rearm != 0 && P->rearm != 1) || (P->heavy_first != 0 && P->heavy_first != 1))
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan rearm and heavy_first must be 0 or 1");
+  if (P->rearm == 0 && d != 128)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan rearm = 0 exists for head_dim 128 only");
+  P->tiles = ref.tiles;
+  if (P->split_k == 0) {
+    P->tail_tiles = 0;
+  } else {
+    const int64_t blocks = (keys + piper::kKeyBlock - 1) / piper::kKeyBlock;
+    if (causal) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "the split-KV tail applies to non-causal launches only");
+    if (!split_region)
+      return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan splits keys but the workspace has no split region");
+    if (P->tiles >= (int64_t(1) << 30))
+      return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "too many tiles for a split-KV tail");
+    if (P->split_k < 2 || P->split_k > piper::kMaxSplits || P->split_k > blocks)
+      return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan split_k must be 0 or in [2, min(" +
+                                                       std::to_string(piper::kMaxSplits) + ", key blocks)]");
+    if (P->tail_tiles <= 0 || P->tail_tiles > P->tiles || P->tail_tiles * P->split_k > split_units_max)
+      return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan tail_tiles must be in [1, tiles] with tail_tiles * split_k <= " +
+                                                       std::to_string(split_units_max));
+  }
+  P->ctas = P->tiles - P->tail_tiles + P->tail_tiles * P->split_k;
+  P->kernels = P->split_k > 0 ? 2 : 1;
+  return PIPER_B200_OK;
+}
+
 // The attention launch shared by the one-shot and the sharded entry points:
 // Q side (codes, scales, V mean) from `workspace`, K/V side from `kv_pack`
 // (a K/V pack laid out as in the workspace of the same shape).  The workspace
@@ -240,7 +351,8 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
 int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq_all, int64_t q_row0, int64_t q_rows,
                   int64_t nk_all, int64_t key0, int64_t keys, int64_t head_dim, double scale, int is_causal,
                   const void* workspace, size_t workspace_bytes, const void* kv_pack, int64_t causal_shift,
-                  float* state, int state_mode, void* stream, bool sharded = false) {
+                  float* state, int state_mode, void* stream, bool sharded = false,
+                  const piper_b200_plan_t* plan_in = nullptr) {
   // Sharded causal attention pairs independent query and key shards: only the
   // one-shard form needs Nq == Nk.
   int rc = check_shape(dtype, batch, heads, nq_all, nk_all, head_dim, sharded ? 0 : is_causal);
@@ -304,27 +416,27 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   p.nq_all = nq_all;
   p.q_row0 = q_row0;
   p.k_key0 = key0;
-  // Work units: every tile whole, except that the tiles of a last partial
-  // wave may be cut into key ranges (split-KV tail) so that the wave ends
-  // sooner; merge_split_kernel then combines their partial states (and the
-  // carried state, which key range 0 starts from).  Only for non-causal
-  // launches, and when the workspace has the optional split region.
-  const int64_t tiles = static_cast<int64_t>(p.q_tiles) * bh;
-  p.main_units = tiles;
-  p.splits = 0;
-  p.split_units = 0;
-  p.split_state = reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + L.split_state);
+  // Work units: every tile whole, except that the plan may cut the trailing
+  // tiles into key ranges (split-KV tail) whose partial states
+  // merge_split_kernel then combines (key range 0 starts from any carried
+  // state).
   const int sms = g_device_sms[device] > 0 ? g_device_sms[device] : 148;
-  if (!is_causal && workspace_bytes >= L.total_bytes && tiles < (int64_t(1) << 30)) {
-    const int64_t tail = tiles % sms;
-    const int64_t blocks = (keys + piper::kKeyBlock - 1) / piper::kKeyBlock;
-    const int64_t k = tail > 0 ? std::min<int64_t>({int64_t(piper::kMaxSplits), sms / tail, blocks / 2}) : 0;
-    if (k >= 2 && tail * k <= L.split_units_max) {
-      p.main_units = tiles - tail;
-      p.splits = static_cast<int>(k);
-      p.split_units = tail * k;
-    }
+  const bool split_region = workspace_bytes >= L.total_bytes;
+  piper_b200_plan_t plan;
+  if (plan_in != nullptr) {
+    plan = *plan_in;
+    if ((rc = check_plan(&plan, bh, q_rows, keys, head_dim, is_causal != 0, split_region, L.split_units_max)) !=
+        PIPER_B200_OK)
+      return rc;
+  } else {
+    plan = make_plan(bh, q_rows, keys, head_dim, is_causal != 0, sms, split_region, L.split_units_max);
   }
+  p.reverse_tiles = plan.heavy_first;
+  const int64_t tiles = static_cast<int64_t>(p.q_tiles) * bh;
+  p.main_units = tiles - plan.tail_tiles;
+  p.splits = plan.split_k;
+  p.split_units = plan.tail_tiles * plan.split_k;
+  p.split_state = reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + L.split_state);
   const int64_t units = p.main_units + p.split_units;
   const dim3 grid = units < (int64_t(1) << 31) ? dim3(static_cast<unsigned>(units), 1)
                                                 : dim3(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
@@ -336,7 +448,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
       piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__half, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
     } else {
-      if (is_causal)
+      if (plan.rearm)
         piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       else
         piper::piper_attention_kernel<__half, 128, false, false>
@@ -348,7 +460,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
       piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
     } else {
-      if (is_causal)
+      if (plan.rearm)
         piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
       else
         piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>
@@ -364,7 +476,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
 
 extern "C" {
 
-int piper_b200_abi_version(void) { return 103; }
+int piper_b200_abi_version(void) { return 104; }
 
 const char* piper_b200_last_error(void) { return g_last_error.c_str(); }
 
@@ -415,6 +527,42 @@ int piper_b200_attention_prepared(void* out, int dtype, int64_t batch, int64_t h
   return run_attention(out, dtype, batch, heads, query_length, 0, query_length, key_length, 0, key_length, head_dim,
                        scale, is_causal, workspace, workspace_bytes, static_cast<const uint8_t*>(workspace) + L.kv_pack,
                        0, nullptr, 0, stream);
+}
+
+int piper_b200_select_plan(int64_t batch, int64_t heads, int64_t query_length, int64_t key_length,
+                           int64_t head_dim, int is_causal, int sms, int split_region, piper_b200_plan_t* plan) {
+  if (plan == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if (batch <= 0 || heads <= 0 || query_length <= 0 || key_length <= 0)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "head_dim must be 64 or 128, got " + std::to_string(head_dim));
+  if (sms < 0) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "sms must be non-negative");
+  if (sms == 0) {
+    int device = 0;
+    sms = 148;
+    if (cudaGetDevice(&device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+      cudaGetLastError();
+      sms = 148;
+    }
+  }
+  const piper_b200_workspace_layout_t L = piper::make_layout(batch * heads, query_length, key_length, head_dim);
+  *plan = make_plan(batch * heads, query_length, key_length, head_dim, is_causal != 0, sms, split_region != 0,
+                    L.split_units_max);
+  return PIPER_B200_OK;
+}
+
+int piper_b200_attention_prepared_plan(void* out, int dtype, int64_t batch, int64_t heads, int64_t query_length,
+                                       int64_t key_length, int64_t head_dim, double scale, int is_causal,
+                                       const void* workspace, size_t workspace_bytes, const piper_b200_plan_t* plan,
+                                       void* stream) {
+  if (!out || !workspace || !plan) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+  int rc = check_shape(dtype, batch, heads, query_length, key_length, head_dim, is_causal);
+  if (rc != PIPER_B200_OK) return rc;
+  const piper_b200_workspace_layout_t L = piper::make_layout(batch * heads, query_length, key_length, head_dim);
+  return run_attention(out, dtype, batch, heads, query_length, 0, query_length, key_length, 0, key_length, head_dim,
+                       scale, is_causal, workspace, workspace_bytes, static_cast<const uint8_t*>(workspace) + L.kv_pack,
+                       0, nullptr, 0, stream, false, plan);
 }
 
 int piper_b200_shard_column_sums(const void* key, const int64_t key_strides[3], const void* value,
@@ -566,16 +714,22 @@ namespace {
 static __device__ __align__(256) uint8_t g_no_alloc_workspace[PIPER_B200_NO_ALLOC_WORKSPACE_BYTES];
 
 void* g_no_alloc_address[kMaxDevices] = {};
+unsigned long long g_no_alloc_context[kMaxDevices] = {};  // context the address belongs to
 
+// The array's device address in the current context of `device` (which
+// ensure_device made current).  Looked up once per context: a reset device
+// gets a new context, a new copy of the array and so a new address.
 int no_alloc_workspace(int device, void** ptr) {
   std::lock_guard<std::mutex> lock(g_init_mutex);
-  if (g_no_alloc_address[device] == nullptr) {
+  const unsigned long long context = current_context_id();
+  if (g_no_alloc_address[device] == nullptr || context == 0 || g_no_alloc_context[device] != context) {
     void* address = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&address, g_no_alloc_workspace);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc workspace)");
     if (address == nullptr || reinterpret_cast<uintptr_t>(address) % 256 != 0)
       return fail(PIPER_B200_ERR_CUDA, "no-alloc workspace has no usable device address");
     g_no_alloc_address[device] = address;
+    g_no_alloc_context[device] = context;
   }
   *ptr = g_no_alloc_address[device];
   return PIPER_B200_OK;
@@ -640,22 +794,32 @@ struct HostPlan {
 // overlap.
 constexpr double kHostChunkBytes = 52e6;
 
+// At most kMaxTailChunks chunks carry the remainder after the bulk chunks.
+constexpr int64_t kMaxTailChunks = 16;
+
 void make_host_plan(int64_t bh, int64_t nq, int64_t nk, int64_t d, int sms, HostPlan* P) {
   const int64_t q_tiles = (nq + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles);
   const double head_bytes = static_cast<double>((nq + 2 * nk) * d * 2);
   const int64_t max_hc = std::max<int64_t>(1, std::min<int64_t>(16, bh / 3));
   int64_t hc = std::max<int64_t>(1, std::min<int64_t>(max_hc, std::llround(kHostChunkBytes / head_bytes)));
-  hc = std::max<int64_t>(hc, (bh + kMaxHostChunks - 3) / (kMaxHostChunks - 2));
+  // The chunk count is bounded: one first chunk, at most
+  // kMaxHostChunks - 1 - kMaxTailChunks bulk chunks, at most kMaxTailChunks
+  // remainder chunks.
+  hc = std::max<int64_t>(hc, (bh + kMaxHostChunks - 2 - kMaxTailChunks) / (kMaxHostChunks - 1 - kMaxTailChunks));
   const int64_t per_wave = std::max<int64_t>(1, std::min<int64_t>(hc, sms / std::max<int64_t>(q_tiles, 1)));
   int64_t n = 0, h = 0;
   auto add = [&](int64_t heads) {
+    if (n >= kMaxHostChunks) return;  // unreachable with the bounds above; never write past the arrays
     P->chunk_h0[n] = h;
     P->chunk_heads[n++] = heads;
     h += heads;
   };
   add(std::min<int64_t>(per_wave, bh));
   while (bh - h > hc) add(hc);
-  while (h < bh) add(std::min<int64_t>(per_wave, bh - h));
+  // The remainder (at most hc heads) in one-wave chunks, or in
+  // kMaxTailChunks equal chunks when one-wave chunks would be more.
+  const int64_t tail_chunk = std::max<int64_t>(per_wave, (bh - h + kMaxTailChunks - 1) / kMaxTailChunks);
+  while (h < bh && n < kMaxHostChunks) add(std::min<int64_t>(tail_chunk, bh - h));
   P->chunks = n;
   P->heads_per_slot = hc;
   P->q_bytes = static_cast<uint64_t>(hc * nq * d) * 2;
@@ -679,6 +843,7 @@ void make_host_plan(int64_t bh, int64_t nq, int64_t nk, int64_t d, int sms, Host
 
 struct HostStreams {
   bool ready = false;
+  unsigned long long context = 0;  // the context the streams and events belong to
   cudaStream_t h2d = nullptr, d2h = nullptr, compute = nullptr;
   cudaEvent_t start = nullptr;
   cudaEvent_t loaded[kHostSlots] = {}, computed[kHostSlots] = {}, drained[kHostSlots] = {};
@@ -689,7 +854,10 @@ HostStreams g_host[kMaxDevices];
 int host_streams(int device, HostStreams** out) {
   std::lock_guard<std::mutex> lock(g_init_mutex);
   HostStreams& h = g_host[device];
-  if (!h.ready) {
+  // Streams and events die with their context (a device reset): make new ones then.
+  const unsigned long long context = current_context_id();
+  if (!h.ready || context == 0 || h.context != context) {
+    h.ready = false;
     PIPER_CUDA(cudaStreamCreateWithFlags(&h.h2d, cudaStreamNonBlocking));
     PIPER_CUDA(cudaStreamCreateWithFlags(&h.d2h, cudaStreamNonBlocking));
     PIPER_CUDA(cudaStreamCreateWithFlags(&h.compute, cudaStreamNonBlocking));
@@ -700,6 +868,7 @@ int host_streams(int device, HostStreams** out) {
       PIPER_CUDA(cudaEventCreateWithFlags(&h.drained[i], cudaEventDisableTiming));
     }
     h.ready = true;
+    h.context = context;
   }
   *out = &h;
   return PIPER_B200_OK;
@@ -935,6 +1104,7 @@ extern "C" int piper_b200_sage2pp_attention_prepared(void* out, int dtype, int64
   p.nk_pad = L.nk_pad;
   p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
   p.causal = is_causal ? 1 : 0;
+  p.reverse_tiles = p.causal;
   p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
   p.wait_budget_ns = piper::kWaitBudgetNs;
   p.nq_all = query_length;

@@ -12,12 +12,8 @@ import ctypes
 import threading
 from pathlib import Path
 
-import os
-
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
-# PIPER_B200_LIBRARY may point at another build of the same ABI (used to
-# compare kernel variants side by side); the default is the in-tree build.
-LIB_PATH = Path(os.environ.get("PIPER_B200_LIBRARY", LIB_DIR / "libpiper_b200.so"))
+LIB_PATH = LIB_DIR / "libpiper_b200.so"
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1
@@ -41,6 +37,8 @@ EXPORTED_SYMBOLS = (
     "piper_b200_prepass",
     "piper_b200_attention_prepared",
     "piper_b200_attention_fwd",
+    "piper_b200_select_plan",
+    "piper_b200_attention_prepared_plan",
     "piper_b200_attention_fwd_no_alloc",
     "piper_b200_shard_column_sums",
     "piper_b200_shard_prepass",
@@ -76,6 +74,15 @@ class WorkspaceLayout(ctypes.Structure):
     ] + [(name, ctypes.c_int64) for name in ("q_groups", "k_groups", "nk_pad", "chunks")] + [
         (name, ctypes.c_uint64) for name in ("kv_pack", "kv_pack_bytes", "totals", "split_state")
     ] + [("split_units_max", ctypes.c_int64)]
+
+
+class Plan(ctypes.Structure):
+    """Mirror of ``piper_b200_plan_t``."""
+
+    _fields_ = [(name, ctypes.c_int32) for name in ("tile_rows", "key_block", "stages", "rearm", "heavy_first",
+                                                     "split_k")] + [
+        (name, ctypes.c_int64) for name in ("tiles", "tail_tiles", "ctas")
+    ] + [(name, ctypes.c_int32) for name in ("kernels", "sms")]
 
 
 class Sage2ppLayout(ctypes.Structure):
@@ -119,6 +126,12 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, _VP,
     ]
     lib.piper_b200_attention_fwd.restype = ctypes.c_int
+    lib.piper_b200_select_plan.argtypes = [_I64] * 5 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Plan)]
+    lib.piper_b200_select_plan.restype = ctypes.c_int
+    lib.piper_b200_attention_prepared_plan.argtypes = [_VP, ctypes.c_int] + [_I64] * 5 + [
+        ctypes.c_double, ctypes.c_int, _VP, ctypes.c_size_t, ctypes.POINTER(Plan), _VP,
+    ]
+    lib.piper_b200_attention_prepared_plan.restype = ctypes.c_int
     lib.piper_b200_attention_fwd_no_alloc.argtypes = tensor3 + [_VP, ctypes.c_int] + [_I64] * 5 + [
         ctypes.c_double, ctypes.c_int, _VP,
     ]

@@ -18,6 +18,9 @@ import torch
 class AcceleratorTarget:
     backend: str
     architecture: str | None = None
+    # Streaming multiprocessors: the launch plan sizes its waves by it (148 on a
+    # B200; tests build targets with other counts).
+    multi_processor_count: int | None = None
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "backend", self.backend.strip().lower())
@@ -31,7 +34,8 @@ class AcceleratorTarget:
         if getattr(torch.version, "hip", None) is not None:
             return cls(backend="hip", architecture=getattr(torch.cuda.get_device_properties(device), "gcnArchName", None))
         major, minor = torch.cuda.get_device_capability(device)
-        return cls(backend="cuda", architecture=f"sm{major}{minor}")
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        return cls(backend="cuda", architecture=f"sm{major}{minor}", multi_processor_count=sms)
 
     @property
     def cuda_capability(self) -> tuple[int, int] | None:

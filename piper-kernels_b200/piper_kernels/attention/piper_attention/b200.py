@@ -18,10 +18,14 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
+from typing import TYPE_CHECKING
 
 import torch
 
 from ... import _native
+
+if TYPE_CHECKING:
+    from ._policy import PiperAttentionExecutionPlan
 
 _DTYPE_CODES = {torch.float16: _native.FLOAT16, torch.bfloat16: _native.BFLOAT16}
 
@@ -155,27 +159,51 @@ def prepare_piper_attention(
     return PreparedPiperAttention(workspace, layout, (b, h, nq, nk, d), query.dtype, is_causal)
 
 
+def default_execution_plan(prepared: PreparedPiperAttention) -> "PiperAttentionExecutionPlan":
+    """The plan ``launch_piper_attention`` uses for ``prepared`` on its device."""
+    from ..._targets import AcceleratorTarget
+    from ._policy import select_execution_plan
+
+    b, h, nq, nk, d = prepared.shape
+    return select_execution_plan(
+        AcceleratorTarget.from_device(prepared.workspace.device), batch=b, heads=h, query_length=nq,
+        key_length=nk, head_dim=d, is_causal=prepared.is_causal,
+        split_region=prepared.workspace.numel() >= int(prepared.layout.total_bytes),
+    )
+
+
 def launch_piper_attention(
     prepared: PreparedPiperAttention,
     scale: float,
     *,
     out: torch.Tensor | None = None,
+    plan: "PiperAttentionExecutionPlan | None" = None,
 ) -> torch.Tensor:
-    """Run only the fused attention kernel on a prepared workspace."""
+    """Run only the fused attention kernel on a prepared workspace.
+
+    ``plan`` overrides the production execution plan (the offline tuner's
+    candidates); by default the library selects it.
+    """
     lib = _native.library()
     b, h, nq, nk, d = prepared.shape
     device = prepared.workspace.device
     if out is None:
         out = torch.empty((b, h, nq, d), dtype=prepared.dtype, device=device)
     with torch.cuda.device(device):
-        _native.check(
-            lib.piper_b200_attention_prepared(
+        if plan is None:
+            status = lib.piper_b200_attention_prepared(
                 _ptr(out), _DTYPE_CODES[prepared.dtype], b, h, nq, nk, d, float(scale),
                 1 if prepared.is_causal else 0, _ptr(prepared.workspace), prepared.workspace.numel(),
                 _stream(device),
-            ),
-            "piper_b200_attention_prepared",
-        )
+            )
+        else:
+            native_plan = plan.to_native()
+            status = lib.piper_b200_attention_prepared_plan(
+                _ptr(out), _DTYPE_CODES[prepared.dtype], b, h, nq, nk, d, float(scale),
+                1 if prepared.is_causal else 0, _ptr(prepared.workspace), prepared.workspace.numel(),
+                ctypes.byref(native_plan), _stream(device),
+            )
+        _native.check(status, "piper_b200_attention_prepared")
     return out
 
 

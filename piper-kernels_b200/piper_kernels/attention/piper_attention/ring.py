@@ -34,6 +34,7 @@ library.  Tests substitute a CPU restatement to exercise this host logic over
 
 from __future__ import annotations
 
+import datetime
 from typing import Callable, Protocol
 
 import torch
@@ -47,6 +48,24 @@ OPERATOR = "ring_piper_attention"
 STATE_LOAD = _native.STATE_LOAD
 STATE_STORE = _native.STATE_STORE
 SHARD_ALIGNMENT = 64  # rows per K quantization group
+
+
+class RingStepError(RuntimeError):
+    """A ring step's exchange with a neighbour failed or did not finish in time.
+
+    Raised on the ranks that survive a peer which left (raised, exited or
+    hung) before finishing the ring.  With ``abort_on_failure`` the group has
+    been aborted, so no collective of it is left waiting on the dead peer.
+    """
+
+
+def _abort(group) -> None:
+    """Abort the group's communicators, where the backend supports it."""
+    pg = group if group is not None else dist.distributed_c10d._get_default_group()
+    try:
+        pg.abort()
+    except (RuntimeError, NotImplementedError, AttributeError):
+        pass
 
 
 class ShardOps(Protocol):
@@ -211,6 +230,8 @@ def ring_piper_attention(
     group: dist.ProcessGroup | None = None,
     layout: str = "contiguous",
     ops_factory: Callable[..., ShardOps] | None = None,
+    step_timeout: datetime.timedelta | None = None,
+    abort_on_failure: bool = False,
 ) -> torch.Tensor:
     """Piper Attention of a sequence sharded over ``group`` (this rank's rows).
 
@@ -222,6 +243,15 @@ def ring_piper_attention(
     Without an initialised process group it is ``piper_attention`` on one GPU.
     ``layout`` is "contiguous" or "zigzag" (see the module docstring; with
     "zigzag" the shard length must be a multiple of 128).
+
+    Failure handling: by default each ring step's send/receive is ordered on
+    the device stream (no host wait), and a peer that leaves is caught by the
+    process group's own timeout.  With ``step_timeout`` the host instead waits
+    for every step's exchange, at most that long (the backend's blocking wait
+    with a timeout), and raises :class:`RingStepError` naming the step and the
+    neighbours when it fails or runs out -- before this rank launches anything
+    of the next step.  ``abort_on_failure`` then also aborts the group's
+    communicators, so that no collective stays waiting on the lost peer.
     """
     if layout not in ("contiguous", "zigzag"):
         raise ValueError(f"{OPERATOR} layout must be 'contiguous' or 'zigzag', got {layout!r}")
@@ -283,7 +313,22 @@ def ring_piper_attention(
             ops.attend(held, state, mode, shift if masked else 0, out, query_range=query_range, key_range=key_range,
                        masked=masked)
         for work in pending:
-            work.wait()
+            if step_timeout is None:
+                work.wait()
+                continue
+            try:
+                completed = work.wait(step_timeout)
+            except Exception as exc:  # the backend's timeout or a broken connection
+                if abort_on_failure:
+                    _abort(group)
+                raise RingStepError(
+                    f"{OPERATOR}: rank {rank}, ring step {step}: the K/V exchange with ranks {to_rank}/{from_rank} "
+                    f"failed or did not finish within {step_timeout.total_seconds():g} s ({exc})"
+                ) from exc
+            if completed is False:
+                if abort_on_failure:
+                    _abort(group)
+                raise RingStepError(f"{OPERATOR}: rank {rank}, ring step {step}: the K/V exchange did not complete")
         if not last:
             held = incoming
     return out

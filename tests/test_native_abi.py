@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol() -> None:
 
 
 def test_abi_version() -> None:
-    assert _native.library().piper_b200_abi_version() == 103
+    assert _native.library().piper_b200_abi_version() == 104
 
 
 def test_workspace_layout_regions_are_aligned_and_disjoint() -> None:

@@ -240,3 +240,93 @@ def test_single_process_ring_is_the_one_shot_operator() -> None:
         out = ring_piper_attention(q, k, v, is_causal=True, ops_factory=OracleShardOps)
     expected = oracle.piper_attention_torch(q, k, v, None, True)
     assert torch.equal(out, expected)
+
+
+class SimulatedRankFailure(RuntimeError):
+    """The host-made failure of the leaving rank."""
+
+
+class FailingShardOps(OracleShardOps):
+    """Oracle ops that fail on one rank: before the ring ("quantize") or in its second step ("attend")."""
+
+    fail_rank = -1
+    fail_at = ""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.attends = 0
+
+    def quantize(self, total_keys):
+        if dist.get_rank() == self.fail_rank and self.fail_at == "quantize":
+            raise SimulatedRankFailure("rank leaves after the totals all-reduce")
+        super().quantize(total_keys)
+
+    def attend(self, *args, **kwargs):
+        self.attends += 1
+        if dist.get_rank() == self.fail_rank and self.fail_at == "attend" and self.attends == 1:
+            raise SimulatedRankFailure("rank leaves in ring step 0, before forwarding any pack")
+        super().attend(*args, **kwargs)
+
+
+def _leaving_worker(rank: int, world: int, port: int, fail_at: str, then: str, results) -> None:
+    import datetime
+    import time
+
+    from piper_kernels.attention.piper_attention.ring import RingStepError
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    oracle.set_threads(1)
+    FailingShardOps.fail_rank, FailingShardOps.fail_at = 1, fail_at
+    q, k, v = _inputs(128 * world, 64, torch.float16)
+    rows = slice(rank * 128, (rank + 1) * 128)
+    t0 = time.monotonic()
+    try:
+        with torch.no_grad():
+            out = ring_piper_attention(q[:, :, rows], k[:, :, rows], v[:, :, rows], ops_factory=FailingShardOps,
+                                       step_timeout=datetime.timedelta(seconds=3), abort_on_failure=True)
+        # A survivor may finish when every pack it needs had already left the
+        # departed rank; its rows must then be right.
+        expected = oracle.piper_attention_torch(q, k, v, None, False)[:, :, rows]
+        results[rank] = ("finished" if torch.equal(out, expected) else "wrong", time.monotonic() - t0)
+    except SimulatedRankFailure:
+        results[rank] = ("left", time.monotonic() - t0)
+        if then == "hang":
+            time.sleep(12)  # alive but silent: the others must give up on their own clock
+        return  # leave without tearing the group down
+    except RingStepError:
+        results[rank] = ("raised", time.monotonic() - t0)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_at", ["quantize", "attend"])
+@pytest.mark.parametrize("then", ["exit", "hang"])
+def test_surviving_ranks_raise_when_a_rank_leaves_the_ring(fail_at: str, then: str) -> None:
+    # A rank that fails on the host between ring steps (SURVEY: failure
+    # detection without a GPU fault): every other rank raises RingStepError
+    # within the step timeout instead of waiting forever.
+    world = 3
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        procs = [ctx.Process(target=_leaving_worker, args=(r, world, _free_port() if r < 0 else port, fail_at, then,
+                                                           results))
+                 for port in [_free_port()] for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=90)
+        alive = [p.pid for p in procs if p.is_alive()]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert not alive, f"ranks still running: {alive}"
+        outcome = dict(results)
+    assert outcome[1][0] == "left"
+    survivors = [outcome[r] for r in (0, 2)]
+    assert all(status in ("raised", "finished") and seconds < 30 for status, seconds in survivors), outcome
+    # Without rank 1 after the totals, nobody gets its pack; failing in step 0
+    # it forwards nothing, so at least its successor cannot finish.
+    if fail_at == "quantize":
+        assert all(status == "raised" for status, _ in survivors), outcome
+    assert outcome[2][0] == "raised", outcome
