@@ -136,9 +136,10 @@ typedef struct piper_b200_plan_s {
   int32_t tile_rows;   /* query rows per CTA (two 128-row tiles) */
   int32_t key_block;   /* keys per online-softmax block */
   int32_t stages;      /* depth of the kernel's K/V shared-memory ring */
-  int32_t rearm;       /* 1: the S accumulators are re-armed with the bias pattern after each read;
-                          0: the first QK^T step overwrites them and the bias is added in registers
-                          (an instance that exists for D=128 only) */
+  int32_t rearm;       /* 1: the S accumulators are re-armed with the bias pattern after each read
+                          and the probabilities go through shared memory;
+                          0: the first QK^T step overwrites S, the bias is added in registers and
+                          the probabilities are written into TMEM over the spent scores */
   int32_t heavy_first; /* causal: query tiles with the most visible keys are scheduled first */
   int32_t split_k;     /* key ranges per tile of the split-KV tail; 0 = no split */
   int64_t tiles;       /* query tiles of the launch: B*H*ceil(Nq / tile_rows) */
@@ -160,8 +161,8 @@ int piper_b200_select_plan(int64_t batch, int64_t heads, int64_t query_length, i
 /* piper_b200_attention_prepared with an explicit plan (from
  * piper_b200_select_plan, possibly edited: rearm, heavy_first, split_k and
  * tail_tiles are honoured; tiles, ctas and kernels are recomputed).  Plans
- * that the kernels cannot run (a split for causal attention, rearm 0 at D=64,
- * more split CTAs than the workspace's split region holds) are rejected with
+ * that the kernels cannot run (a split for causal attention, more split CTAs
+ * than the workspace's split region holds) are rejected with
  * PIPER_B200_ERR_INVALID_ARGUMENT. */
 int piper_b200_attention_prepared_plan(void* out, int dtype, int64_t batch, int64_t heads,
                                        int64_t query_length, int64_t key_length, int64_t head_dim,
@@ -331,6 +332,13 @@ int piper_b200_device_status(int device, int clear, uint32_t* status);
  * mbarrier nothing ever arrives at, with a `budget_ns` limit, and reports
  * whether it gave up cleanly (*timed_out = 1) while the context stays usable. */
 int piper_b200_selftest_wait_timeout(uint64_t budget_ns, int* timed_out, void* stream);
+
+/* Self-test of the kernels' software exp2 (the FMA-pipe polynomial that
+ * takes a share of the probabilities off the MUFU unit): y[i] = 2^x[i] as the
+ * attention kernel computes it, and ex2[i] = the hardware ex2.approx of the
+ * same x (either output may be NULL).  x, y and ex2 are device float arrays of
+ * n elements; tests compare both against exact 2^x. */
+int piper_b200_selftest_exp2(const float* x, float* y, float* ex2, int64_t n, void* stream);
 
 /* Diagnostic GEMM on the tensor cores: C[M,N] (int32) = A[M,K] * B[N,K]^T with
  * A u8 or s8 (a_signed), B s8, both K-major, through the same TMA + tcgen05

@@ -90,7 +90,7 @@ struct AttnSmem {
   static constexpr int kOffP = kOffV + kStages * kVBytes;
   static constexpr int kOffVec = kOffP + kTiles * 2 * kPBytes;
   static constexpr int kOffBar = kOffVec + kStages * kVecBytes;
-  static constexpr int kNumBars = 1 + 2 * kStages + 3 * kTiles * 2 + kTiles + 1;
+  static constexpr int kNumBars = 1 + 2 * kStages + 3 * kTiles * 2 + kTiles + 1 + 2 * kTiles;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
@@ -493,11 +493,20 @@ constexpr float kPScale = 32.0f;
 // rounding per probability: the code bits c from the +1.5*2^23 add are placed
 // under an fp16 exponent (2 + c/512), and one HFMA2 with the power-of-two
 // multiples 512*w and -1024*w of the fp16 weight w gives c*w.
-// kRearm: the S accumulators are re-armed with the bias pattern by the
-// softmax (tcgen05.st) after each read; otherwise the first QK^T K-step
-// overwrites them and the bias bits are added in registers.  Measured: not
-// re-arming is 2% faster for non-causal D=128 launches, and 2% (causal) to 5%
-// (D=64) slower elsewhere; the host picks the instance per launch.
+// kRearm selects one of two instances:
+//  - true: the S accumulators are re-armed with the bias pattern by the
+//    softmax (tcgen05.st) after each read, and the weighted codes go to a
+//    128B-swizzled shared-memory tile that the PV MMA reads;
+//  - false: the first QK^T K-step overwrites S and the bias bits are added in
+//    registers; the weighted codes are written into TMEM over the block's
+//    spent score columns (32 columns of fp16 pairs) and the PV MMA reads its
+//    A operand from there.  No shared-memory P store and no async-proxy
+//    fence; the S buffer is handed back by the PV MMA itself (the issuer puts
+//    the next QK^T into it only after that PV, and the tensor pipe runs them
+//    in order), so a block never waits for the previous block's PV before
+//    releasing its P.  PV completions alternate between two barriers per
+//    tile, waited on only for a rescale and at the end.
+// The host picks the instance per launch (the execution plan's `rearm`).
 template <typename T, int D, bool kRearm>
 __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t* smem, uint32_t sbase,
                                                    uint32_t tmem_base, const SoftmaxBars& bars, int nbt, int64_t q0,
@@ -620,8 +629,10 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
       const float w_old = need ? ex2_approx(m_ref - new_ref) : 1.0f;
       if (j >= 1 || load) {
         if (j >= 1 && pv_seen < j) {
-          if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
-                                    bars.abort_flag)))
+          // PV(j - 1) and, in issue order, every earlier PV have completed.
+          const uint32_t pv_bar = kRearm ? bars.pv_full + 8 * t : bars.pv_full + 8 * (2 * t + ((j - 1) & 1));
+          const uint32_t pv_parity = kRearm ? ((j - 1) & 1) : (((j - 1) >> 1) & 1);
+          if (!(ok = mbar_wait_warp(pv_bar, pv_parity, budget, status, kStatusTimeoutMma, bars.abort_flag)))
             break;
           pv_seen = j;
         }
@@ -664,12 +675,14 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
     const float2 kb2 = make_float2(kBias, kBias);
     uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * S::kPVRow;
     const int sw = r & 7;  // 128B swizzle: 16-byte chunk index ^ (row % 8)
+    const uint32_t tm_p = tm_s + buf * kKeyBlock;  // TMEM P: fp16 pairs over the spent scores
+    uint32_t words[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {  // 8 keys per 16-byte chunk
       const float4 ra = lds128(vr + 32 * c), rb = lds128(vr + 32 * c + 16);
       const float2 rv[4] = {make_float2(ra.x, ra.y), make_float2(ra.z, ra.w), make_float2(rb.x, rb.y),
                             make_float2(rb.z, rb.w)};
-      uint32_t words[4];
+      uint32_t* wc = words + 4 * (c & 1);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float2 e = __fadd2_rn(x[4 * c + q], mneg);
@@ -684,15 +697,25 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
         const float2 y = __ffma2_rn(e, k255, kb2);
         uint32_t h = __byte_perm(__float_as_uint(y.x), __float_as_uint(y.y), 0x6420);  // 2 + c/512, twice
         __half2 pw = __hfma2(*reinterpret_cast<__half2*>(&h), w512, w1024n);
-        words[q] = *reinterpret_cast<uint32_t*>(&pw);
+        wc[q] = *reinterpret_cast<uint32_t*>(&pw);
       }
-      *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(words[0], words[1], words[2], words[3]);
+      if constexpr (kRearm) {
+        *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(wc[0], wc[1], wc[2], wc[3]);
+      } else if (c & 1) {
+        tmem_st8(tm_p + 4 * (c - 1), words);  // keys 8(c-1) .. 8c+7: columns 4(c-1) .. 4c+3
+      }
     }
-    fence_proxy_async_shared();
-    // PV of the previous block must have completed before this block's P is
-    // released, so each pv_full phase is consumed before the next can
-    // complete (and the P buffer of block j + 1 is free).
-    if (j >= 1 && pv_seen < j) {
+    if constexpr (kRearm) {
+      fence_proxy_async_shared();
+    } else {
+      tmem_st_wait();
+      tc_fence_before();
+    }
+    // Shared-memory P (re-arm instance): PV of the previous block must have
+    // completed before this block's P is released, so each pv_full phase is
+    // consumed before the next can complete (and the P buffer of block j + 1
+    // is free).
+    if (kRearm && j >= 1 && pv_seen < j) {
       if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
                                 bars.abort_flag)))
         break;
@@ -704,7 +727,9 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
     l_run = fmaf(psum, w_cur, l_run);
   }
   if (ok && nbt > 0) {
-    ok = mbar_wait_warp(bars.pv_full + 8 * t, (nbt - 1) & 1, budget, status, kStatusTimeoutMma, bars.abort_flag);
+    const uint32_t pv_bar = kRearm ? bars.pv_full + 8 * t : bars.pv_full + 8 * (2 * t + ((nbt - 1) & 1));
+    const uint32_t pv_parity = kRearm ? ((nbt - 1) & 1) : (((nbt - 1) >> 1) & 1);
+    ok = mbar_wait_warp(pv_bar, pv_parity, budget, status, kStatusTimeoutMma, bars.abort_flag);
     tc_fence_after();
   }
 
@@ -812,6 +837,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t p_full = s_free + 8 * kTiles * 2;        // [tile][buf]
   const uint32_t pv_full = p_full + 8 * kTiles * 2;       // [tile]
   const uint32_t mma_done = pv_full + 8 * kTiles;
+  const uint32_t pv_half = mma_done + 8;                  // [tile][block parity] (TMEM-P instance)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffMisc);
   const uint32_t abort_flag = sbase + S::kOffMisc + 4;
 
@@ -866,6 +892,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(pv_full + 8 * t, 1);
     }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < 2 * kTiles; ++i) mbar_init(pv_half + 8 * i, 1);
     flag_set(abort_flag, 0u);
     fence_mbarrier_init();
   }
@@ -956,7 +983,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int t = 0; t < kTiles; ++t) {
           const int jq = qk_next[t];
-          if (jq < nb[t] && mbar_test(kv_full + 8 * (jq % kStages), (jq / kStages) & 1) &&
+          // TMEM-P instance: S buffer jq & 1 holds P(jq - 2) until PV(jq - 2)
+          // has read it; issued after that PV, QK(jq) runs after it.
+          if (jq < nb[t] && (kSage || kRearm || pv_next[t] + 1 >= jq) &&
+              mbar_test(kv_full + 8 * (jq % kStages), (jq / kStages) & 1) &&
               mbar_test(s_free + 8 * (t * 2 + (jq & 1)), ((jq >> 1) & 1) ^ 1)) {
             tc_fence_after();
             const uint64_t descK = descK0 + static_cast<uint64_t>(((jq % kStages) * S::kKBytes) >> 4);
@@ -980,15 +1010,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
               for (int kk = 0; kk < kKeyBlock / 32; ++kk)
                 umma_f8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf8, 1u);
-            } else {
+            } else if constexpr (kRearm) {
               // fp16 weighted probabilities x fp16 V codes, 16 keys (32 B) per
               // MMA, accumulated in F32 onto the numerator in TMEM.
               constexpr uint32_t kIdescPVf16 = umma_idesc_f16(kTileM, D);
 #pragma unroll
               for (int kk = 0; kk < kKeyBlock / 16; ++kk)
                 umma_f16(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf16, 1u);
+            } else {
+              // The same with the probabilities read from TMEM (8 columns per
+              // 16 keys) where the softmax wrote them over the spent scores.
+              constexpr uint32_t kIdescPVf16 = umma_idesc_f16(kTileM, D);
+              const uint32_t a_tm = tmem_base + t * 256 + (jp & 1) * kKeyBlock;
+#pragma unroll
+              for (int kk = 0; kk < kKeyBlock / 16; ++kk)
+                umma_f16_ts(dcol, a_tm + 8 * kk, descV + 2 * kk, kIdescPVf16, 1u);
             }
-            umma_commit(pv_full + 8 * t);
+            umma_commit((kSage || kRearm) ? pv_full + 8 * t : pv_half + 8 * (2 * t + (jp & 1)));
             pv_next[t] = jp + 1;
             progress = true;
           }
@@ -1025,7 +1063,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sage_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, status, budget);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, abort_flag};
+    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, kRearm ? pv_full : pv_half, abort_flag};
     piper_softmax_role<T, D, kRearm>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
   }
 
@@ -1164,6 +1202,22 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 64);
+  }
+}
+
+// The software exp2 of the softmax, element by element (self-test).
+__global__ void selftest_exp2_kernel(const float* x, float* y, float* ex2, int64_t n) {
+  const int64_t i = 2 * (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float2 v = make_float2(x[i], i + 1 < n ? x[i + 1] : 0.0f);
+  const float2 e = exp2_poly2(v);
+  if (y != nullptr) {
+    y[i] = e.x;
+    if (i + 1 < n) y[i + 1] = e.y;
+  }
+  if (ex2 != nullptr) {
+    ex2[i] = ex2_approx(v.x);
+    if (i + 1 < n) ex2[i + 1] = ex2_approx(v.y);
   }
 }
 

@@ -114,31 +114,38 @@ int ensure_device(int* device_out) {
   // The attention kernels redistribute registers between warpgroups with
   // setmaxnreg, which is only safe at the launch register count the split was
   // computed for.
-  // Index bit 0: D=128; 2: bf16; 4: SageAttention2++; 8: Piper without S re-arm (D=128).
-  const void* kernels[10] = {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, true>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, true>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, false, false>),
-                             reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>)};
-  for (int i = 0; i < 10; ++i) {
-    // Piper kernels (i < 4) stage 16-bit PV operands; SageAttention2++ 8-bit ones.
-    const int smem_bytes = i >= 8 ? piper::AttnSmem<128, true>::kAlloc
-                           : i < 4 ? ((i % 2 == 0) ? piper::AttnSmem<64, true>::kAlloc : piper::AttnSmem<128, true>::kAlloc)
-                                   : ((i % 2 == 0) ? piper::AttnSmem<64>::kAlloc : piper::AttnSmem<128>::kAlloc);
-    PIPER_CUDA(cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
+  // Piper kernels stage 16-bit PV operands (or keep P in TMEM: the no-re-arm
+  // instances); SageAttention2++ 8-bit ones.
+  struct Instance {
+    const void* fn;
+    int smem;
+  };
+  const Instance kernels[] = {
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>), piper::AttnSmem<64, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>), piper::AttnSmem<128, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>), piper::AttnSmem<64, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>), piper::AttnSmem<128, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, false, false>), piper::AttnSmem<64, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, false, false>), piper::AttnSmem<128, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, false, false>), piper::AttnSmem<64, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>), piper::AttnSmem<128, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, true>), piper::AttnSmem<64>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, true>), piper::AttnSmem<128>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>), piper::AttnSmem<64>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>), piper::AttnSmem<128>::kAlloc},
+  };
+  for (const Instance& k : kernels) {
+    const void* fn = k.fn;
+    const int smem_bytes = k.smem;
+    PIPER_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
     cudaFuncAttributes attr;
-    PIPER_CUDA(cudaFuncGetAttributes(&attr, kernels[i]));
+    PIPER_CUDA(cudaFuncGetAttributes(&attr, fn));
     if (attr.numRegs != piper::kLaunchRegs)
       return fail(PIPER_B200_ERR_CUDA, "attention kernel compiled with " + std::to_string(attr.numRegs) +
                                            " registers per thread; its warpgroup register split needs " +
                                            std::to_string(piper::kLaunchRegs));
     int resident = 0;
-    PIPER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kernels[i], piper::kAttnThreads, smem_bytes));
+    PIPER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fn, piper::kAttnThreads, smem_bytes));
     if (resident < 1)
       return fail(PIPER_B200_ERR_UNSUPPORTED_DEVICE, "an attention CTA does not fit on one SM of this device");
   }
@@ -274,9 +281,10 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
 // Production plan of one attention launch over `q_rows` query rows and `keys`
 // keys per head (pure host logic).  The tile shape and ring depth are fixed by
 // the compiled kernels; the rest are the measured choices:
-//   - rearm: the instance that re-arms the S accumulators with the bias
-//     pattern is 2-5% faster for causal and D=64 launches; for non-causal
-//     D=128 the instance that adds the bias in registers is 2% faster.
+//   - rearm = 0: the instance that adds the score bias in registers and keeps
+//     the probabilities in TMEM is faster for every launch kind (measured
+//     against the re-arm instance with shared-memory probabilities: c4 +4%,
+//     causal c3 +4%, D=64 +11%).
 //   - heavy_first: causal tiles with more visible keys start first.
 //   - split-KV tail: when the tiles do not fill whole waves on the SMs, the
 //     `tail` tiles of the last partial wave are cut into
@@ -289,7 +297,7 @@ piper_b200_plan_t make_plan(int64_t bh, int64_t q_rows, int64_t keys, int64_t d,
   P.tile_rows = piper::kTileM * piper::kTiles;
   P.key_block = piper::kKeyBlock;
   P.stages = d == 128 ? piper::AttnSmem<128, true>::kStages : piper::AttnSmem<64, true>::kStages;
-  P.rearm = (d == 128 && !causal) ? 0 : 1;
+  P.rearm = 0;
   P.heavy_first = causal ? 1 : 0;
   P.sms = sms;
   P.tiles = (q_rows + P.tile_rows - 1) / P.tile_rows * bh;
@@ -319,8 +327,6 @@ int check_plan(piper_b200_plan_t* P, int64_t bh, int64_t q_rows, int64_t keys, i
                                                      std::to_string(ref.stages) + ")");
   if ((P->rearm != 0 && P->rearm != 1) || (P->heavy_first != 0 && P->heavy_first != 1))
     return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan rearm and heavy_first must be 0 or 1");
-  if (P->rearm == 0 && d != 128)
-    return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "plan rearm = 0 exists for head_dim 128 only");
   P->tiles = ref.tiles;
   if (P->split_k == 0) {
     P->tail_tiles = 0;
@@ -341,6 +347,21 @@ int check_plan(piper_b200_plan_t* P, int64_t bh, int64_t q_rows, int64_t keys, i
   P->ctas = P->tiles - P->tail_tiles + P->tail_tiles * P->split_k;
   P->kernels = P->split_k > 0 ? 2 : 1;
   return PIPER_B200_OK;
+}
+
+// The attention kernel instance the plan names (S re-arm with P in shared
+// memory, or no re-arm with P in TMEM), then the split-KV merge if any.
+template <typename T, int D>
+void launch_piper_kernels(const dim3& grid, const dim3& merge_grid, bool rearm, const CUtensorMap& tmQ,
+                          const CUtensorMap& tmK, const CUtensorMap& tmV, const piper::AttnParams& p,
+                          cudaStream_t s) {
+  constexpr int kSmem = piper::AttnSmem<D, true>::kAlloc;
+  if (rearm)
+    piper::piper_attention_kernel<T, D><<<grid, piper::kAttnThreads, kSmem, s>>>(tmQ, tmK, tmV, p);
+  else
+    piper::piper_attention_kernel<T, D, false, false><<<grid, piper::kAttnThreads, kSmem, s>>>(tmQ, tmK, tmV, p);
+  if (p.split_units)
+    piper::merge_split_kernel<T, D><<<merge_grid, piper::kTileM * piper::kTiles, 0, s>>>(p);
 }
 
 // The attention launch shared by the one-shot and the sharded entry points:
@@ -442,31 +463,16 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
                                                 : dim3(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 merge_grid(static_cast<unsigned>(p.split_units > 0 ? p.split_units / p.splits : 0));
-  constexpr unsigned kMergeThreads = piper::kTileM * piper::kTiles;
   if (dtype == PIPER_B200_FLOAT16) {
-    if (head_dim == 64) {
-      piper::piper_attention_kernel<__half, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-      if (p.split_units) piper::merge_split_kernel<__half, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
-    } else {
-      if (plan.rearm)
-        piper::piper_attention_kernel<__half, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-      else
-        piper::piper_attention_kernel<__half, 128, false, false>
-            <<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-      if (p.split_units) piper::merge_split_kernel<__half, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
-    }
+    if (head_dim == 64)
+      launch_piper_kernels<__half, 64>(grid, merge_grid, plan.rearm != 0, tmQ, tmK, tmV, p, s);
+    else
+      launch_piper_kernels<__half, 128>(grid, merge_grid, plan.rearm != 0, tmQ, tmK, tmV, p, s);
   } else {
-    if (head_dim == 64) {
-      piper::piper_attention_kernel<__nv_bfloat16, 64><<<grid, piper::kAttnThreads, piper::AttnSmem<64, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-      if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 64><<<merge_grid, kMergeThreads, 0, s>>>(p);
-    } else {
-      if (plan.rearm)
-        piper::piper_attention_kernel<__nv_bfloat16, 128><<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-      else
-        piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>
-            <<<grid, piper::kAttnThreads, piper::AttnSmem<128, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
-      if (p.split_units) piper::merge_split_kernel<__nv_bfloat16, 128><<<merge_grid, kMergeThreads, 0, s>>>(p);
-    }
+    if (head_dim == 64)
+      launch_piper_kernels<__nv_bfloat16, 64>(grid, merge_grid, plan.rearm != 0, tmQ, tmK, tmV, p, s);
+    else
+      launch_piper_kernels<__nv_bfloat16, 128>(grid, merge_grid, plan.rearm != 0, tmQ, tmK, tmV, p, s);
   }
   PIPER_CUDA(cudaGetLastError());
   return PIPER_B200_OK;
@@ -670,6 +676,20 @@ int piper_b200_selftest_wait_timeout(uint64_t budget_ns, int* timed_out, void* s
   if (d_status) cudaFree(d_status);
   if (e != cudaSuccess) return cuda_fail(e, "wait-timeout self-test");
   *timed_out = (host_flag == 1 && (host_status & piper::kStatusTimeoutProbe)) ? 1 : 0;
+  return PIPER_B200_OK;
+}
+
+int piper_b200_selftest_exp2(const float* x, float* y, float* ex2, int64_t n, void* stream) {
+  if (n < 0 || n > (int64_t(1) << 31)) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "n must be in [0, 2^31]");
+  if (n == 0) return PIPER_B200_OK;
+  if (x == nullptr) return fail(PIPER_B200_ERR_INVALID_ARGUMENT, "x is NULL");
+  int device = 0;
+  int rc = ensure_device(&device);
+  if (rc != PIPER_B200_OK) return rc;
+  const int64_t pairs = (n + 1) / 2;
+  piper::selftest_exp2_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, ex2, n);
+  PIPER_CUDA(cudaGetLastError());
   return PIPER_B200_OK;
 }
 

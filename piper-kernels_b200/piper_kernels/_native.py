@@ -54,6 +54,7 @@ EXPORTED_SYMBOLS = (
     "piper_b200_sage2pp_fwd",
     "piper_b200_device_status",
     "piper_b200_selftest_wait_timeout",
+    "piper_b200_selftest_exp2",
     "piper_b200_selftest_gemm_i8",
 )
 
@@ -178,6 +179,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.piper_b200_device_status.restype = ctypes.c_int
     lib.piper_b200_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int), _VP]
     lib.piper_b200_selftest_wait_timeout.restype = ctypes.c_int
+    lib.piper_b200_selftest_exp2.argtypes = [_VP, _VP, _VP, _I64, _VP]
+    lib.piper_b200_selftest_exp2.restype = ctypes.c_int
     lib.piper_b200_selftest_gemm_i8.argtypes = [_VP, _VP, _VP] + [_I64] * 3 + [ctypes.c_int, _VP]
     lib.piper_b200_selftest_gemm_i8.restype = ctypes.c_int
 

@@ -15,9 +15,10 @@ Fields (see ``piper_b200_plan_t``):
   (two 128-row query tiles per CTA, 64-key softmax blocks, the K/V
   shared-memory ring depth); reported, not chosen;
 * ``rearm`` -- kernel instance: re-arm the INT32 score accumulators with the
-  float bias pattern after each read (faster for causal and D=64 launches),
-  or let the first QK^T step overwrite them and add the bias in registers
-  (faster for non-causal D=128);
+  float bias pattern after each read and pass the probabilities to the PV
+  MMA through shared memory, or let the first QK^T step overwrite them, add
+  the bias in registers and write the probabilities into TMEM over the spent
+  scores, where the PV MMA reads them;
 * ``heavy_first`` -- causal launches schedule the query tiles with the most
   visible keys first;
 * ``split_k`` / ``tail_tiles`` -- the split-KV tail: the trailing tiles of a

@@ -49,7 +49,7 @@ def test_every_candidate_plan_computes_the_same_attention(shape, dtype, causal) 
         prepared = prepare_piper_attention(qd, kd, vd, causal)
         production = default_execution_plan(prepared)
         base = launch_piper_attention(prepared, d**-0.5)
-        plans = candidate_plans(production, rearm=[False, True] if d == 128 else None, heavy_first=[False, True],
+        plans = candidate_plans(production, rearm=[False, True], heavy_first=[False, True],
                                 split_k=None if causal else [0, 2, 3, 8])
         outs = []
         for plan in plans:
@@ -73,8 +73,8 @@ def test_plans_the_kernels_cannot_run_are_refused() -> None:
     with torch.no_grad():
         prepared = prepare_piper_attention(q, k, v, True)
         production = default_execution_plan(prepared)
-        with pytest.raises(ValueError, match="head_dim 128 only"):
-            launch_piper_attention(prepared, 0.125, plan=production.with_choices(rearm=False))
+        with pytest.raises(ValueError, match="fixed by the kernels"):
+            launch_piper_attention(prepared, 0.125, plan=production.__class__(**{**production.as_dict(), "stages": 3}))
         with pytest.raises(ValueError, match="non-causal launches only"):
             launch_piper_attention(prepared, 0.125, plan=production.with_choices(split_k=2, tail_tiles=1))
 

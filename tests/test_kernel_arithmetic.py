@@ -69,3 +69,35 @@ def test_int8_codes_convert_to_fp16_exactly() -> None:
         word = byte_perm(u | (u << 8) | (u << 16) | (u << 24), 0x64646464, 0x5140)
         h = halves(word).astype(np.float32)
         assert h[0] - 1152.0 == c and h[1] - 1152.0 == c
+
+
+def test_polynomial_exp2_emulated_in_fp32() -> None:
+    # CPU restatement of exp2_poly2 (csrc/attention.cuh): each Horner step an
+    # fp32 fused multiply-add (emulated through fp64 products); the stated
+    # relative-error bound holds over [-125, 0], and below -125 the result is
+    # tiny and non-negative.
+    import numpy as np
+
+    coeffs = [np.float32(c) for c in (0.001327644451521337, 0.00967553723603487, 0.05550713464617729,
+                                      0.24022120237350464, 0.6931469440460205, 1.0000001192092896)]
+
+    def fma(a, b, c):
+        return (np.float64(a) * np.float64(b) + np.float64(c)).astype(np.float32)
+
+    def poly(x):
+        x = np.maximum(x, np.float32(-126.5)).astype(np.float32)
+        t = (x + np.float32(12582912.0)).astype(np.float32)
+        u = (t - np.float32(12582912.0)).astype(np.float32)
+        f = fma(u, np.float32(-1.0), x)
+        p = fma(coeffs[0], f, coeffs[1])
+        for c in coeffs[2:]:
+            p = fma(p, f, c)
+        bits = (t.view(np.uint32).astype(np.uint64) * 0x800000 + p.view(np.uint32).astype(np.uint64)) & 0xFFFFFFFF
+        return bits.astype(np.uint32).view(np.float32)
+
+    x = np.linspace(-125.0, 0.0, 1_000_001).astype(np.float32)
+    exact = np.exp2(x.astype(np.float64))
+    rel = np.abs(poly(x).astype(np.float64) - exact) / exact
+    assert rel.max() <= 2.5e-7
+    tiny = poly(np.array([-np.inf, -300.0, -126.0], dtype=np.float32)).astype(np.float64)
+    assert (tiny >= 0).all() and (tiny <= 2.0**-124).all()

@@ -55,13 +55,15 @@ def test_split_depends_on_the_sm_count() -> None:
 def test_causal_plan_has_no_split_and_heavy_tiles_first() -> None:
     plan = _select(batch=4, heads=32, n=8192, causal=True)
     assert plan.split_k == 0 and plan.tail_tiles == 0 and plan.kernels == 1
-    assert plan.rearm and plan.heavy_first
+    assert plan.heavy_first
 
 
-def test_rearm_instance_choice() -> None:
+def test_tmem_probability_instance_everywhere() -> None:
+    # The no-re-arm instance (probabilities in TMEM) is the production choice
+    # for every head dimension and mask.
     assert not _select(d=128).rearm
-    assert _select(d=64).rearm
-    assert _select(d=128, causal=True).rearm
+    assert not _select(d=64).rearm
+    assert not _select(d=128, causal=True).rearm
 
 
 def test_no_split_without_the_workspace_region_or_short_keys() -> None:
