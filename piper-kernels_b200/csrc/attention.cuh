@@ -28,9 +28,9 @@
 //                    row i = TMEM lane i)
 //   warp 8           TMA producer: Q tiles once, then K, V^T tiles and the
 //                    per-key log2(vs), 1/vs vectors into a K/V ring
-//   warp 9           TMEM allocator + single-thread tcgen05.mma issuer,
-//                    event driven: QK^T and PV of each tile issued as soon
-//                    as their operands are ready
+//   warp 9           TMEM allocator + the QK^T issuer (one thread)
+//   warp 10          the PV issuer (one thread); both event driven: each MMA
+//                    issued as soon as its operands are ready
 // Shared-memory operands are in the canonical 128B/64B-swizzled K-major
 // layouts TMA writes; P is written by the softmax threads into the same
 // 128B-swizzled layout.  No multicast anywhere.  The SageAttention2++ kernel
@@ -891,7 +891,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(pv_full + 8 * t, 1);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);  // one commit per issuing thread
     for (int i = 0; i < 2 * kTiles; ++i) mbar_init(pv_half + 8 * i, 1);
     flag_set(abort_flag, 0u);
     fence_mbarrier_init();
@@ -960,13 +960,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int j = max(0, issued - kStages); j < issued; ++j)
         mbar_wait(kv_full + 8 * (j % kStages), (j / kStages) & 1, budget, status, kStatusTimeoutDrain, 0u);
       mbar_wait(q_full, 0, budget, status, kStatusTimeoutDrain, 0u);
-    } else if (warp == 9 && lane == 0) {
-      // ------------------------------------------------ MMA issuer
+    } else if ((warp == 9 || warp == 10) && lane == 0) {
+      // ------------------------------------------------ MMA issuers
+      // Two issuing threads: warp 9 issues every QK^T, warp 10 every PV.  One
+      // thread issuing both was the kernel's bottleneck (measured: each
+      // tcgen05.mma costs its issuing thread about 80-200 cycles, and a block
+      // needs 16 of them), so the scores arrived late; split, each stream of
+      // MMAs advances on its own (c4 929 -> 1049 TOPS).
       // Event driven: each tile advances on its own.  QK^T of block j needs
-      // the K/V stage loaded and the S buffer released by the softmax; PV of
-      // block j needs its P (it accumulates onto the numerator in TMEM).
-      // Whatever is ready is issued; a stage is released to the producer once
-      // every tile has issued its PV for that block.
+      // the K/V stage loaded and the S buffer released by the softmax (for the
+      // TMEM-P instance also PV(j - 2) completed: P(j - 2) lives in that
+      // buffer, and the two threads' MMAs are not ordered with each other);
+      // PV of block j needs its P (it accumulates onto the numerator in TMEM).
+      // A stage is released to the producer by the PV thread once every tile
+      // has issued its PV for that block (QK(j) has completed before P(j)
+      // exists, so the PV thread's commit covers both readers of the stage).
+      const bool qk_role = warp == 9;
       constexpr uint32_t kIdescQK = umma_idesc_i8(true, true, kTileM, kKeyBlock);
       bool ok = mbar_wait(q_full, 0, budget, status, kStatusTimeoutFull, abort_flag);
       tc_fence_after();
@@ -983,9 +992,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int t = 0; t < kTiles; ++t) {
           const int jq = qk_next[t];
-          // TMEM-P instance: S buffer jq & 1 holds P(jq - 2) until PV(jq - 2)
-          // has read it; issued after that PV, QK(jq) runs after it.
-          if (jq < nb[t] && (kSage || kRearm || pv_next[t] + 1 >= jq) &&
+          if (qk_role && jq < nb[t] &&
+              (kSage || kRearm || jq < 2 || mbar_test(pv_half + 8 * (2 * t + (jq & 1)), ((jq - 2) >> 1) & 1)) &&
               mbar_test(kv_full + 8 * (jq % kStages), (jq / kStages) & 1) &&
               mbar_test(s_free + 8 * (t * 2 + (jq & 1)), ((jq >> 1) & 1) ^ 1)) {
             tc_fence_after();
@@ -1000,7 +1008,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           const int jp = pv_next[t];
           // PV accumulates in TMEM across blocks: no accumulator to wait for.
-          if (jp < qk_next[t] && mbar_test(p_full + 8 * (t * 2 + (jp & 1)), (jp >> 1) & 1)) {
+          if (!qk_role && jp < nb[t] && mbar_test(p_full + 8 * (t * 2 + (jp & 1)), (jp >> 1) & 1)) {
             tc_fence_after();
             const uint64_t descV = descV0 + static_cast<uint64_t>(((jp % kStages) * S::kVBytes) >> 4);
             const uint64_t descP = descP0 + static_cast<uint64_t>(((t * 2 + (jp & 1)) * S::kPBytes) >> 4);
@@ -1031,12 +1039,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             progress = true;
           }
         }
-        while (released < nb_max && (released >= nb[0] || pv_next[0] > released) &&
+        while (!qk_role && released < nb_max && (released >= nb[0] || pv_next[0] > released) &&
                (released >= nb[1] || pv_next[1] > released)) {
           umma_commit(kv_empty + 8 * (released % kStages));
           ++released;
         }
-        if (released >= nb_max) break;
+        if (qk_role ? (qk_next[0] >= nb[0] && qk_next[1] >= nb[1]) : released >= nb_max) break;
         if (progress) {
           idle_since = 0;
         } else {
@@ -1053,7 +1061,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           __nanosleep(32);
         }
       }
-      // Everything issued must complete before TMEM is freed.
+      // Everything issued (by both threads: two arrivals) must complete
+      // before TMEM is freed.
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, budget, status, kStatusTimeoutMma, 0u);
     }

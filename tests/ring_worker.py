@@ -2,7 +2,8 @@
 
 Every rank builds the same full sequence from one seed, runs
 ``ring_piper_attention`` on its rows over NCCL, and compares them with the
-one-GPU operator on the whole sequence, computed on its own GPU.  Prints
+one-GPU operator on the whole sequence, computed on its own GPU, and head 0
+with the CPU oracle on the same tensors.  Prints
 RING_OK on success; any mismatch raises (non-zero exit).
 """
 
@@ -20,6 +21,7 @@ for _p in (REPO / "piper-kernels_b200", REPO):
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
+from oracle import oracle  # noqa: E402
 from piper_kernels import piper_attention  # noqa: E402
 from piper_kernels.attention.piper_attention import ring_piper_attention  # noqa: E402
 from piper_kernels.attention.piper_attention.ring import zigzag_shard  # noqa: E402
@@ -46,14 +48,24 @@ def main() -> None:
             else:
                 def mine_of(t):
                     return t[:, :, rank * n_shard : (rank + 1) * n_shard]
+            # The last case also waits for every ring step on the host (the
+            # failure-detection path), which must not change the result.
+            timeout = datetime.timedelta(seconds=30) if layout == "zigzag" else None
             with torch.no_grad():
-                mine = ring_piper_attention(mine_of(q), mine_of(k), mine_of(v), is_causal=is_causal, layout=layout)
+                mine = ring_piper_attention(mine_of(q), mine_of(k), mine_of(v), is_causal=is_causal, layout=layout,
+                                            step_timeout=timeout, abort_on_failure=timeout is not None)
                 whole = mine_of(piper_attention(q, k, v, is_causal=is_causal))
             torch.cuda.synchronize()
             err = (mine.float() - whole.float()).abs()
             if not (err.max().item() < 0.02 and err.mean().item() < 2e-4):
                 raise AssertionError(f"rank {rank} causal={is_causal} {layout}: max {err.max().item()} "
                                      f"mean {err.mean().item()}")
+            # Head 0 against the oracle on the same tensors (the reference's GPU bounds).
+            expected = oracle.piper_attention_torch(q[:, :1].cpu(), k[:, :1].cpu(), v[:, :1].cpu(), 128**-0.5,
+                                                    is_causal).float()
+            ref_err = (mine[:, :1].float().cpu() - mine_of(expected)).abs()
+            if not (ref_err.mean().item() < 0.003 and ref_err.max().item() < 0.12):
+                raise AssertionError(f"rank {rank} causal={is_causal} {layout} vs oracle: max {ref_err.max().item()}")
         dist.barrier(device_ids=[local])
         print("RING_OK", rank, flush=True)
     finally:
