@@ -140,7 +140,8 @@ typedef struct piper_b200_plan_s {
                           and the probabilities go through shared memory;
                           0: the first QK^T step overwrites S, the bias is added in registers and
                           the probabilities are written into TMEM over the spent scores */
-  int32_t heavy_first; /* causal: query tiles with the most visible keys are scheduled first */
+  int32_t heavy_first; /* causal: longest-work-first grid order across all heads (every head's
+                          last query tile first, then every head's second-to-last, ...) */
   int32_t split_k;     /* key ranges per tile of the split-KV tail; 0 = no split */
   int64_t tiles;       /* query tiles of the launch: B*H*ceil(Nq / tile_rows) */
   int64_t tail_tiles;  /* trailing tiles cut into split_k key ranges (0 when split_k is 0) */

@@ -109,8 +109,9 @@ struct AttnParams {
   int64_t heads, nq, nk, nk_pad, q_groups, k_groups;
   float scale_log2e;
   int causal;
-  int reverse_tiles;  // schedule query tiles last-first (causal: heaviest first)
+  int reverse_tiles;  // heaviest-first tile order (causal): see tile_coords
   int q_tiles;  // ceil(Nq / 256)
+  int64_t bh_count;  // B*H of the launch
   uint64_t wait_budget_ns;
   // Sequence shards.  Causal visibility is key <= query + causal_shift in
   // shard-local indices (causal_shift = first query position - first key
@@ -229,6 +230,22 @@ __device__ __forceinline__ WorkUnit decode_unit(const AttnParams& p) {
     w.split = static_cast<int>(u % p.splits);
   }
   return w;
+}
+
+// Tile index -> (b*h, query tile).  In order, query tiles run fastest within a
+// head.  With reverse_tiles (causal launches, where a query tile's work grows
+// with its position), the query tile is the slow index, counted down: every
+// head's last query tile comes first, then every head's second-to-last, and so
+// on -- the longest-work-first order in which whole-grid scheduling balances
+// best, also when the grid is only a few waves (a few heads per GPU).
+__device__ __forceinline__ void tile_coords(const AttnParams& p, int64_t tile, int64_t& bh, int& qt) {
+  if (p.reverse_tiles) {
+    bh = tile % p.bh_count;
+    qt = p.q_tiles - 1 - static_cast<int>(tile / p.bh_count);
+  } else {
+    bh = tile / p.q_tiles;
+    qt = static_cast<int>(tile % p.q_tiles);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -735,7 +752,9 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
 
   // Recomputed here rather than kept live through the loop.
   const WorkUnit we = decode_unit(p);
-  const int64_t bh_e = we.tile / p.q_tiles;
+  int64_t bh_e;
+  int qt_e;
+  tile_coords(p, we.tile, bh_e, qt_e);
   const bool store = we.split >= 0 || (p.state_mode & kStateStore);
   // Every lane takes part in the TMEM loads (warp-collective); only valid
   // rows write.
@@ -846,10 +865,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // Work unit -> (tile, key range).  Tiles run query-tile fastest.
   const WorkUnit wu = decode_unit(p);
   const int split = wu.split;  // >= 0: this CTA is key range `split` of a tail tile
-  const int64_t bh = wu.tile / p.q_tiles;
-  const int qtl = static_cast<int>(wu.tile % p.q_tiles);
-  // Causal work grows with the query position: the plan hands out heavy tiles first.
-  const int qt = p.reverse_tiles ? (p.q_tiles - 1 - qtl) : qtl;
+  int64_t bh;
+  int qt;
+  tile_coords(p, wu.tile, bh, qt);
   const int64_t q0 = static_cast<int64_t>(qt) * kTileM * kTiles;
   int64_t key0 = p.k_key0;  // first key of this CTA's range
   int64_t nk_cta = p.nk;
@@ -1095,9 +1113,10 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const AttnParams p) {
   const int64_t st = blockIdx.x;
   const int64_t tile = p.main_units + st;
-  const int64_t bh = tile / p.q_tiles;
-  const int64_t qtl = tile % p.q_tiles;  // same tile order as the attention kernel
-  const int64_t row = (p.reverse_tiles ? (p.q_tiles - 1 - qtl) : qtl) * (kTileM * kTiles) + threadIdx.x;
+  int64_t bh;
+  int qt;
+  tile_coords(p, tile, bh, qt);  // same tile order as the attention kernel
+  const int64_t row = static_cast<int64_t>(qt) * (kTileM * kTiles) + threadIdx.x;
   if (row >= p.nq) return;
   constexpr int kRows = kTileM * kTiles;
   const float2* ml = reinterpret_cast<const float2*>(p.split_state + p.split_units * kRows * D);

@@ -285,7 +285,7 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
 //     the probabilities in TMEM is faster for every launch kind (measured
 //     against the re-arm instance with shared-memory probabilities: c4 +4%,
 //     causal c3 +4%, D=64 +11%).
-//   - heavy_first: causal tiles with more visible keys start first.
+//   - heavy_first: causal grids run longest-work-first across all heads.
 //   - split-KV tail: when the tiles do not fill whole waves on the SMs, the
 //     `tail` tiles of the last partial wave are cut into
 //     k = min(kMaxSplits, SMs / tail, key blocks / 2) key ranges, so that the
@@ -453,6 +453,7 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
     plan = make_plan(bh, q_rows, keys, head_dim, is_causal != 0, sms, split_region, L.split_units_max);
   }
   p.reverse_tiles = plan.heavy_first;
+  p.bh_count = bh;
   const int64_t tiles = static_cast<int64_t>(p.q_tiles) * bh;
   p.main_units = tiles - plan.tail_tiles;
   p.splits = plan.split_k;
@@ -1125,6 +1126,7 @@ extern "C" int piper_b200_sage2pp_attention_prepared(void* out, int dtype, int64
   p.scale_log2e = static_cast<float>(scale * 1.4426950408889634);
   p.causal = is_causal ? 1 : 0;
   p.reverse_tiles = p.causal;
+  p.bh_count = bh;
   p.q_tiles = static_cast<int>((query_length + piper::kTileM * piper::kTiles - 1) / (piper::kTileM * piper::kTiles));
   p.wait_budget_ns = piper::kWaitBudgetNs;
   p.nq_all = query_length;
