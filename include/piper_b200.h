@@ -135,11 +135,14 @@ int piper_b200_attention_fwd(const void* query, const int64_t query_strides[3], 
 typedef struct piper_b200_plan_s {
   int32_t tile_rows;   /* query rows per CTA (two 128-row tiles) */
   int32_t key_block;   /* keys per online-softmax block */
-  int32_t stages;      /* depth of the kernel's K/V shared-memory ring */
-  int32_t rearm;       /* 1: the S accumulators are re-armed with the bias pattern after each read
-                          and the probabilities go through shared memory;
-                          0: the first QK^T step overwrites S, the bias is added in registers and
-                          the probabilities are written into TMEM over the spent scores */
+  int32_t stages;      /* depth of the production kernel's K/V shared-memory ring, in iterations
+                          of 128 keys */
+  int32_t rearm;       /* 0: the production kernel: 128 keys (two blocks) per iteration with
+                          N = 128 QK^T MMAs, the bias added in registers and the probabilities
+                          written into TMEM over the spent scores;
+                          1: the 64-key-block kernel that re-arms the S accumulators with the
+                          bias pattern after each read and passes the probabilities through
+                          shared memory */
   int32_t heavy_first; /* causal: longest-work-first grid order across all heads (every head's
                           last query tile first, then every head's second-to-last, ...) */
   int32_t split_k;     /* key ranges per tile of the split-KV tail; 0 = no split */

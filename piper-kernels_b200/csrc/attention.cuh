@@ -23,19 +23,23 @@
 // INT32 block sum.  The lazy rescale (m' moves by more than 2^8) scales O in
 // TMEM.
 //
-// CTA = 384 threads, one CTA per SM (TMEM: all 512 columns):
+// This file holds what the attention kernels share (parameters, work units,
+// tile order, constants, the row epilogue) and the 64-key-block kernel,
+// block64_attention_kernel, which runs SageAttention2++ and the re-arm form of
+// Piper Attention.  The production Piper kernel, with 128 keys per iteration,
+// is piper_attention.cuh.  block64_attention_kernel: CTA = 384 threads, one
+// CTA per SM (TMEM: all 512 columns):
 //   warpgroup 0 / 1  softmax for Q tile 0 / 1 (128 rows each; thread i owns
 //                    row i = TMEM lane i)
 //   warp 8           TMA producer: Q tiles once, then K, V^T tiles and the
-//                    per-key log2(vs), 1/vs vectors into a K/V ring
+//                    per-key vectors into a K/V ring
 //   warp 9           TMEM allocator + the QK^T issuer (one thread)
 //   warp 10          the PV issuer (one thread); both event driven: each MMA
 //                    issued as soon as its operands are ready
 // Shared-memory operands are in the canonical 128B/64B-swizzled K-major
 // layouts TMA writes; P is written by the softmax threads into the same
-// 128B-swizzled layout.  No multicast anywhere.  The SageAttention2++ kernel
-// (kSage) shares this skeleton with e4m3 P/V and a per-block F32 partial.
-//
+// swizzled layout.  No multicast anywhere.
+
 // Sequence shards (ring attention): the recurrence above is associative over
 // key blocks, so a launch may cover one shard of the keys and carry each
 // row's (O, m, l) in a state buffer to the launch over the next shard
@@ -90,7 +94,7 @@ struct AttnSmem {
   static constexpr int kOffP = kOffV + kStages * kVBytes;
   static constexpr int kOffVec = kOffP + kTiles * 2 * kPBytes;
   static constexpr int kOffBar = kOffVec + kStages * kVecBytes;
-  static constexpr int kNumBars = 1 + 2 * kStages + 3 * kTiles * 2 + kTiles + 1 + 2 * kTiles;
+  static constexpr int kNumBars = 1 + 2 * kStages + 3 * kTiles * 2 + kTiles + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
@@ -501,6 +505,99 @@ __device__ __forceinline__ void scores_to_x(const uint32_t (&a)[32], const uint3
 // operand and the constants below within fp16 range.
 constexpr float kPScale = 32.0f;
 
+// Writes one softmax thread's query row once its last PV MMA has completed:
+// the output O / (kPScale * max(l, 1e-30)) + mean_V (reference.py:116-118),
+// or, for a split-tail CTA or under kStateStore, the bias-free carried state
+// (O / kPScale, reference max, denominator).  `run` is false after a failed
+// wait or an abort (nothing is written); `any` is false when the row saw no
+// key and carried no state (the empty recurrence: output = mean_V, state =
+// zeros).  Every lane takes part in the TMEM loads (warp-collective); only
+// valid rows write.
+template <typename T, int D>
+__device__ __forceinline__ void write_row_result(const AttnParams& p, uint32_t tm_o, int t, int r, bool valid_row,
+                                                 int64_t grow, float m_ref, float l_run, bool run, bool any) {
+  // Recomputed here rather than kept live through the main loop.
+  const WorkUnit we = decode_unit(p);
+  int64_t bh_e;
+  int qt_e;
+  tile_coords(p, we.tile, bh_e, qt_e);
+  const bool store = we.split >= 0 || (p.state_mode & kStateStore);
+  if (run && any) {
+    const bool write = valid_row;
+    float4* so = nullptr;
+    uint4* orow = nullptr;
+    const float* vm = p.vmean + bh_e * D;
+    float inv = 0.0f;
+    if (store) {
+      if (we.split >= 0) {
+        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
+        so = reinterpret_cast<float4*>(p.split_state + slot * D);
+        if (write) reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D)[slot] =
+            make_float2(m_ref, l_run);
+      } else {
+        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow) * D);
+        if (write) reinterpret_cast<float2*>(p.state_ml)[bh_e * p.nq_all + grow] = make_float2(m_ref, l_run);
+      }
+    } else {
+      inv = (1.0f / kPScale) / fmaxf(l_run, 1e-30f);
+      orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow) * D);
+    }
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t v[32];
+      __syncwarp();
+      tmem_ld32_split(tm_o + 32 * c, v);
+      tmem_ld_wait();
+      if (!write) {
+      } else if (store) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          so[8 * c + i] = make_float4(__uint_as_float(v[4 * i]) * (1.0f / kPScale),
+                                      __uint_as_float(v[4 * i + 1]) * (1.0f / kPScale),
+                                      __uint_as_float(v[4 * i + 2]) * (1.0f / kPScale),
+                                      __uint_as_float(v[4 * i + 3]) * (1.0f / kPScale));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm + 32 * c) + 2 * i);
+          const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm + 32 * c) + 2 * i + 1);
+          const float* o = reinterpret_cast<const float*>(v) + 8 * i;
+          uint4 pk;
+          pk.x = pack2<T>(fmaf(o[0], inv, m0.x), fmaf(o[1], inv, m0.y));
+          pk.y = pack2<T>(fmaf(o[2], inv, m0.z), fmaf(o[3], inv, m0.w));
+          pk.z = pack2<T>(fmaf(o[4], inv, m1.x), fmaf(o[5], inv, m1.y));
+          pk.w = pack2<T>(fmaf(o[6], inv, m1.z), fmaf(o[7], inv, m1.w));
+          orow[4 * c + i] = pk;
+        }
+      }
+    }
+  } else if (run && valid_row) {
+    // No visible key and no carried state: an empty recurrence.
+    if (store) {
+      float4* so;
+      float2* sml;
+      if (we.split >= 0) {
+        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
+        so = reinterpret_cast<float4*>(p.split_state + slot * D);
+        sml = reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D) + slot;
+      } else {
+        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow) * D);
+        sml = reinterpret_cast<float2*>(p.state_ml) + bh_e * p.nq_all + grow;
+      }
+      for (int i = 0; i < D / 4; ++i) so[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      *sml = make_float2(m_ref, l_run);
+    } else {
+      const float* vm = p.vmean + bh_e * D;
+      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow) * D);
+      for (int c = 0; c < D / 8; ++c) {
+        const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);
+        const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c + 1);
+        orow[c] = make_uint4(pack2<T>(m0.x, m0.y), pack2<T>(m0.z, m0.w), pack2<T>(m1.x, m1.y), pack2<T>(m1.z, m1.w));
+      }
+    }
+  }
+}
+
 // Piper softmax warpgroups (reference.py:61-118): thread i of warpgroup t owns
 // query row i of tile t (TMEM lane i).  Per 64-key block it converts the
 // INT32 scores, takes the block max, applies the lazy rescale, and writes the
@@ -510,21 +607,12 @@ constexpr float kPScale = 32.0f;
 // rounding per probability: the code bits c from the +1.5*2^23 add are placed
 // under an fp16 exponent (2 + c/512), and one HFMA2 with the power-of-two
 // multiples 512*w and -1024*w of the fp16 weight w gives c*w.
-// kRearm selects one of two instances:
-//  - true: the S accumulators are re-armed with the bias pattern by the
-//    softmax (tcgen05.st) after each read, and the weighted codes go to a
-//    128B-swizzled shared-memory tile that the PV MMA reads;
-//  - false: the first QK^T K-step overwrites S and the bias bits are added in
-//    registers; the weighted codes are written into TMEM over the block's
-//    spent score columns (32 columns of fp16 pairs) and the PV MMA reads its
-//    A operand from there.  No shared-memory P store and no async-proxy
-//    fence; the S buffer is handed back by the PV MMA itself (the issuer puts
-//    the next QK^T into it only after that PV, and the tensor pipe runs them
-//    in order), so a block never waits for the previous block's PV before
-//    releasing its P.  PV completions alternate between two barriers per
-//    tile, waited on only for a rescale and at the end.
-// The host picks the instance per launch (the execution plan's `rearm`).
-template <typename T, int D, bool kRearm>
+// This is the re-arm form (the execution plan's `rearm = 1`): the S
+// accumulators are re-armed with the bias pattern by the softmax (tcgen05.st)
+// after each read, and the weighted codes go to a 128B-swizzled
+// shared-memory tile that the PV MMA reads.  The production form, with 128
+// keys per iteration and the probabilities in TMEM, is piper_attention.cuh.
+template <typename T, int D>
 __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t* smem, uint32_t sbase,
                                                    uint32_t tmem_base, const SoftmaxBars& bars, int nbt, int64_t q0,
                                                    int64_t bh, int split, int64_t key0, uint32_t* status,
@@ -601,12 +689,10 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
       tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
       tmem_ld_wait();
       const uint32_t vl = sbase + S::kOffVec + s * S::kVecBytes;
-      if constexpr (kRearm) {
-        // Re-arm the S buffer; s_free is signalled after the block max, by
-        // which time this store has long completed.
-        tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
-      }
-      scores_to_x<!kRearm>(a, b, x, c_row * ks, vl);
+      // Re-arm the S buffer; s_free is signalled after the block max, by
+      // which time this store has long completed.
+      tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
+      scores_to_x<false>(a, b, x, c_row * ks, vl);
     }
     if (p.causal) {
       // Keys after this row are masked (reference.py:86-91); only the
@@ -647,9 +733,8 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
       if (j >= 1 || load) {
         if (j >= 1 && pv_seen < j) {
           // PV(j - 1) and, in issue order, every earlier PV have completed.
-          const uint32_t pv_bar = kRearm ? bars.pv_full + 8 * t : bars.pv_full + 8 * (2 * t + ((j - 1) & 1));
-          const uint32_t pv_parity = kRearm ? ((j - 1) & 1) : (((j - 1) >> 1) & 1);
-          if (!(ok = mbar_wait_warp(pv_bar, pv_parity, budget, status, kStatusTimeoutMma, bars.abort_flag)))
+          if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
+                                    bars.abort_flag)))
             break;
           pv_seen = j;
         }
@@ -692,14 +777,13 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
     const float2 kb2 = make_float2(kBias, kBias);
     uint8_t* prow = smem + S::kOffP + (t * 2 + buf) * S::kPBytes + r * S::kPVRow;
     const int sw = r & 7;  // 128B swizzle: 16-byte chunk index ^ (row % 8)
-    const uint32_t tm_p = tm_s + buf * kKeyBlock;  // TMEM P: fp16 pairs over the spent scores
-    uint32_t words[8];
+    uint32_t words[4];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {  // 8 keys per 16-byte chunk
       const float4 ra = lds128(vr + 32 * c), rb = lds128(vr + 32 * c + 16);
       const float2 rv[4] = {make_float2(ra.x, ra.y), make_float2(ra.z, ra.w), make_float2(rb.x, rb.y),
                             make_float2(rb.z, rb.w)};
-      uint32_t* wc = words + 4 * (c & 1);
+      uint32_t* wc = words;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float2 e = __fadd2_rn(x[4 * c + q], mneg);
@@ -716,23 +800,13 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
         __half2 pw = __hfma2(*reinterpret_cast<__half2*>(&h), w512, w1024n);
         wc[q] = *reinterpret_cast<uint32_t*>(&pw);
       }
-      if constexpr (kRearm) {
-        *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(wc[0], wc[1], wc[2], wc[3]);
-      } else if (c & 1) {
-        tmem_st8(tm_p + 4 * (c - 1), words);  // keys 8(c-1) .. 8c+7: columns 4(c-1) .. 4c+3
-      }
+      *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) = make_uint4(wc[0], wc[1], wc[2], wc[3]);
     }
-    if constexpr (kRearm) {
-      fence_proxy_async_shared();
-    } else {
-      tmem_st_wait();
-      tc_fence_before();
-    }
-    // Shared-memory P (re-arm instance): PV of the previous block must have
-    // completed before this block's P is released, so each pv_full phase is
-    // consumed before the next can complete (and the P buffer of block j + 1
-    // is free).
-    if (kRearm && j >= 1 && pv_seen < j) {
+    fence_proxy_async_shared();
+    // PV of the previous block must have completed before this block's P is
+    // released, so each pv_full phase is consumed before the next can
+    // complete (and the P buffer of block j + 1 is free).
+    if (j >= 1 && pv_seen < j) {
       if (!(ok = mbar_wait_warp(bars.pv_full + 8 * t, (j - 1) & 1, budget, status, kStatusTimeoutMma,
                                 bars.abort_flag)))
         break;
@@ -744,99 +818,19 @@ __device__ __forceinline__ void piper_softmax_role(const AttnParams& p, uint8_t*
     l_run = fmaf(psum, w_cur, l_run);
   }
   if (ok && nbt > 0) {
-    const uint32_t pv_bar = kRearm ? bars.pv_full + 8 * t : bars.pv_full + 8 * (2 * t + ((nbt - 1) & 1));
-    const uint32_t pv_parity = kRearm ? ((nbt - 1) & 1) : (((nbt - 1) >> 1) & 1);
-    ok = mbar_wait_warp(pv_bar, pv_parity, budget, status, kStatusTimeoutMma, bars.abort_flag);
+    ok = mbar_wait_warp(bars.pv_full + 8 * t, (nbt - 1) & 1, budget, status, kStatusTimeoutMma, bars.abort_flag);
     tc_fence_after();
   }
 
-  // Recomputed here rather than kept live through the loop.
-  const WorkUnit we = decode_unit(p);
-  int64_t bh_e;
-  int qt_e;
-  tile_coords(p, we.tile, bh_e, qt_e);
-  const bool store = we.split >= 0 || (p.state_mode & kStateStore);
-  // Every lane takes part in the TMEM loads (warp-collective); only valid
-  // rows write.
-  if (ok && flag_get(bars.abort_flag) == 0 && (nbt > 0 || load)) {
-    const bool write = valid_row;
-    float4* so = nullptr;
-    uint4* orow = nullptr;
-    const float* vm = p.vmean + bh_e * D;
-    float inv = 0.0f;
-    if (store) {
-      if (we.split >= 0) {
-        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
-        so = reinterpret_cast<float4*>(p.split_state + slot * D);
-        if (write) reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D)[slot] =
-            make_float2(m_ref, l_run);
-      } else {
-        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow) * D);
-        if (write) reinterpret_cast<float2*>(p.state_ml)[bh_e * p.nq_all + grow] = make_float2(m_ref, l_run);
-      }
-    } else {
-      inv = (1.0f / kPScale) / fmaxf(l_run, 1e-30f);
-      orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow) * D);
-    }
-#pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t v[32];
-      __syncwarp();
-      tmem_ld32_split(tm_o + 32 * c, v);
-      tmem_ld_wait();
-      if (!write) {
-      } else if (store) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          so[8 * c + i] = make_float4(__uint_as_float(v[4 * i]) * (1.0f / kPScale),
-                                      __uint_as_float(v[4 * i + 1]) * (1.0f / kPScale),
-                                      __uint_as_float(v[4 * i + 2]) * (1.0f / kPScale),
-                                      __uint_as_float(v[4 * i + 3]) * (1.0f / kPScale));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm + 32 * c) + 2 * i);
-          const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm + 32 * c) + 2 * i + 1);
-          const float* o = reinterpret_cast<const float*>(v) + 8 * i;
-          uint4 pk;
-          pk.x = pack2<T>(fmaf(o[0], inv, m0.x), fmaf(o[1], inv, m0.y));
-          pk.y = pack2<T>(fmaf(o[2], inv, m0.z), fmaf(o[3], inv, m0.w));
-          pk.z = pack2<T>(fmaf(o[4], inv, m1.x), fmaf(o[5], inv, m1.y));
-          pk.w = pack2<T>(fmaf(o[6], inv, m1.z), fmaf(o[7], inv, m1.w));
-          orow[4 * c + i] = pk;
-        }
-      }
-    }
-  } else if (ok && flag_get(bars.abort_flag) == 0 && valid_row) {
-    // No visible key and no carried state: an empty recurrence.
-    if (store) {
-      float4* so;
-      float2* sml;
-      if (we.split >= 0) {
-        const int64_t slot = (we.unit - p.main_units) * (kTileM * kTiles) + t * kTileM + r;
-        so = reinterpret_cast<float4*>(p.split_state + slot * D);
-        sml = reinterpret_cast<float2*>(p.split_state + p.split_units * (kTileM * kTiles) * D) + slot;
-      } else {
-        so = reinterpret_cast<float4*>(p.state_o + (bh_e * p.nq_all + grow) * D);
-        sml = reinterpret_cast<float2*>(p.state_ml) + bh_e * p.nq_all + grow;
-      }
-      for (int i = 0; i < D / 4; ++i) so[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      *sml = make_float2(m_ref, l_run);
-    } else {
-      const float* vm = p.vmean + bh_e * D;
-      uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh_e * p.nq_all + grow) * D);
-      for (int c = 0; c < D / 8; ++c) {
-        const float4 m0 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c);
-        const float4 m1 = __ldg(reinterpret_cast<const float4*>(vm) + 2 * c + 1);
-        orow[c] = make_uint4(pack2<T>(m0.x, m0.y), pack2<T>(m0.z, m0.w), pack2<T>(m1.x, m1.y), pack2<T>(m1.z, m1.w));
-      }
-    }
-  }
+  write_row_result<T, D>(p, tm_o, t, r, valid_row, grow, m_ref, l_run,
+                         ok && flag_get(bars.abort_flag) == 0, nbt > 0 || load);
 }
 
-template <typename T, int D, bool kSage = false, bool kRearm = true>
+// The 64-key-block kernel: SageAttention2++ (kSage) and the re-arm form of
+// Piper Attention.
+template <typename T, int D, bool kSage>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    piper_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
+    block64_attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                            const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using S = AttnSmem<D, !kSage>;
@@ -856,7 +850,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t p_full = s_free + 8 * kTiles * 2;        // [tile][buf]
   const uint32_t pv_full = p_full + 8 * kTiles * 2;       // [tile]
   const uint32_t mma_done = pv_full + 8 * kTiles;
-  const uint32_t pv_half = mma_done + 8;                  // [tile][block parity] (TMEM-P instance)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffMisc);
   const uint32_t abort_flag = sbase + S::kOffMisc + 4;
 
@@ -910,7 +903,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(pv_full + 8 * t, 1);
     }
     mbar_init(mma_done, 2);  // one commit per issuing thread
-    for (int i = 0; i < 2 * kTiles; ++i) mbar_init(pv_half + 8 * i, 1);
     flag_set(abort_flag, 0u);
     fence_mbarrier_init();
   }
@@ -986,10 +978,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // needs 16 of them), so the scores arrived late; split, each stream of
       // MMAs advances on its own (c4 929 -> 1049 TOPS).
       // Event driven: each tile advances on its own.  QK^T of block j needs
-      // the K/V stage loaded and the S buffer released by the softmax (for the
-      // TMEM-P instance also PV(j - 2) completed: P(j - 2) lives in that
-      // buffer, and the two threads' MMAs are not ordered with each other);
-      // PV of block j needs its P (it accumulates onto the numerator in TMEM).
+      // the K/V stage loaded and the S buffer released by the softmax; PV of
+      // block j needs its P (it accumulates onto the numerator in TMEM).
       // A stage is released to the producer by the PV thread once every tile
       // has issued its PV for that block (QK(j) has completed before P(j)
       // exists, so the PV thread's commit covers both readers of the stage).
@@ -1011,7 +1001,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int t = 0; t < kTiles; ++t) {
           const int jq = qk_next[t];
           if (qk_role && jq < nb[t] &&
-              (kSage || kRearm || jq < 2 || mbar_test(pv_half + 8 * (2 * t + (jq & 1)), ((jq - 2) >> 1) & 1)) &&
               mbar_test(kv_full + 8 * (jq % kStages), (jq / kStages) & 1) &&
               mbar_test(s_free + 8 * (t * 2 + (jq & 1)), ((jq >> 1) & 1) ^ 1)) {
             tc_fence_after();
@@ -1019,7 +1008,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint32_t dcol = tmem_base + t * 256 + (jq & 1) * kKeyBlock;
 #pragma unroll
             for (int kk = 0; kk < D / 32; ++kk)
-              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, (kk > 0 || kRearm) ? 1u : 0u);
+              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, 1u);
             umma_commit(s_full + 8 * (t * 2 + (jq & 1)));
             qk_next[t] = jq + 1;
             progress = true;
@@ -1036,23 +1025,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
               for (int kk = 0; kk < kKeyBlock / 32; ++kk)
                 umma_f8(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf8, 1u);
-            } else if constexpr (kRearm) {
+            } else {
               // fp16 weighted probabilities x fp16 V codes, 16 keys (32 B) per
               // MMA, accumulated in F32 onto the numerator in TMEM.
               constexpr uint32_t kIdescPVf16 = umma_idesc_f16(kTileM, D);
 #pragma unroll
               for (int kk = 0; kk < kKeyBlock / 16; ++kk)
                 umma_f16(dcol, descP + 2 * kk, descV + 2 * kk, kIdescPVf16, 1u);
-            } else {
-              // The same with the probabilities read from TMEM (8 columns per
-              // 16 keys) where the softmax wrote them over the spent scores.
-              constexpr uint32_t kIdescPVf16 = umma_idesc_f16(kTileM, D);
-              const uint32_t a_tm = tmem_base + t * 256 + (jp & 1) * kKeyBlock;
-#pragma unroll
-              for (int kk = 0; kk < kKeyBlock / 16; ++kk)
-                umma_f16_ts(dcol, a_tm + 8 * kk, descV + 2 * kk, kIdescPVf16, 1u);
             }
-            umma_commit((kSage || kRearm) ? pv_full + 8 * t : pv_half + 8 * (2 * t + (jp & 1)));
+            umma_commit(pv_full + 8 * t);
             pv_next[t] = jp + 1;
             progress = true;
           }
@@ -1090,8 +1071,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sage_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, status, budget);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, kRearm ? pv_full : pv_half, abort_flag};
-    piper_softmax_role<T, D, kRearm>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
+    const SoftmaxBars bars{kv_full, s_full, s_free, p_full, pv_full, abort_flag};
+    piper_softmax_role<T, D>(p, smem, sbase, tmem_base, bars, nb[warp / 4], q0, bh, split, key0, status, budget);
   }
 
   __syncwarp();

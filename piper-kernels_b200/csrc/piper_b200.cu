@@ -15,6 +15,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "piper_attention.cuh"
 #include "layout.h"
 #include "piper_b200.h"
 #include "prepass.cuh"
@@ -114,25 +115,26 @@ int ensure_device(int* device_out) {
   // The attention kernels redistribute registers between warpgroups with
   // setmaxnreg, which is only safe at the launch register count the split was
   // computed for.
-  // Piper kernels stage 16-bit PV operands (or keep P in TMEM: the no-re-arm
-  // instances); SageAttention2++ 8-bit ones.
+  // Piper: the production kernel (128 keys per iteration, P in TMEM) and
+  // the re-arm form of the 64-key-block kernel; SageAttention2++: the
+  // 64-key-block kernel with 8-bit PV operands.
   struct Instance {
     const void* fn;
     int smem;
   };
   const Instance kernels[] = {
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>), piper::AttnSmem<64, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>), piper::AttnSmem<128, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>), piper::AttnSmem<64, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>), piper::AttnSmem<128, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, false, false>), piper::AttnSmem<64, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, false, false>), piper::AttnSmem<128, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, false, false>), piper::AttnSmem<64, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, false, false>), piper::AttnSmem<128, true>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64, true>), piper::AttnSmem<64>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128, true>), piper::AttnSmem<128>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64, true>), piper::AttnSmem<64>::kAlloc},
-      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128, true>), piper::AttnSmem<128>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 64>), piper::PairSmem<64>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__half, 128>), piper::PairSmem<128>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 64>), piper::PairSmem<64>::kAlloc},
+      {reinterpret_cast<const void*>(piper::piper_attention_kernel<__nv_bfloat16, 128>), piper::PairSmem<128>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__half, 64, false>), piper::AttnSmem<64, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__half, 128, false>), piper::AttnSmem<128, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__nv_bfloat16, 64, false>), piper::AttnSmem<64, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__nv_bfloat16, 128, false>), piper::AttnSmem<128, true>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__half, 64, true>), piper::AttnSmem<64>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__half, 128, true>), piper::AttnSmem<128>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__nv_bfloat16, 64, true>), piper::AttnSmem<64>::kAlloc},
+      {reinterpret_cast<const void*>(piper::block64_attention_kernel<__nv_bfloat16, 128, true>), piper::AttnSmem<128>::kAlloc},
   };
   for (const Instance& k : kernels) {
     const void* fn = k.fn;
@@ -296,7 +298,7 @@ piper_b200_plan_t make_plan(int64_t bh, int64_t q_rows, int64_t keys, int64_t d,
   piper_b200_plan_t P{};
   P.tile_rows = piper::kTileM * piper::kTiles;
   P.key_block = piper::kKeyBlock;
-  P.stages = d == 128 ? piper::AttnSmem<128, true>::kStages : piper::AttnSmem<64, true>::kStages;
+  P.stages = d == 128 ? piper::PairSmem<128>::kStages : piper::PairSmem<64>::kStages;
   P.rearm = 0;
   P.heavy_first = causal ? 1 : 0;
   P.sms = sms;
@@ -355,11 +357,11 @@ template <typename T, int D>
 void launch_piper_kernels(const dim3& grid, const dim3& merge_grid, bool rearm, const CUtensorMap& tmQ,
                           const CUtensorMap& tmK, const CUtensorMap& tmV, const piper::AttnParams& p,
                           cudaStream_t s) {
-  constexpr int kSmem = piper::AttnSmem<D, true>::kAlloc;
   if (rearm)
-    piper::piper_attention_kernel<T, D><<<grid, piper::kAttnThreads, kSmem, s>>>(tmQ, tmK, tmV, p);
+    piper::block64_attention_kernel<T, D, false>
+        <<<grid, piper::kAttnThreads, piper::AttnSmem<D, true>::kAlloc, s>>>(tmQ, tmK, tmV, p);
   else
-    piper::piper_attention_kernel<T, D, false, false><<<grid, piper::kAttnThreads, kSmem, s>>>(tmQ, tmK, tmV, p);
+    piper::piper_attention_kernel<T, D><<<grid, piper::kAttnThreads, piper::PairSmem<D>::kAlloc, s>>>(tmQ, tmK, tmV, p);
   if (p.split_units)
     piper::merge_split_kernel<T, D><<<merge_grid, piper::kTileM * piper::kTiles, 0, s>>>(p);
 }
@@ -1137,14 +1139,14 @@ extern "C" int piper_b200_sage2pp_attention_prepared(void* out, int dtype, int64
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == PIPER_B200_FLOAT16) {
     if (head_dim == 64)
-      piper::piper_attention_kernel<__half, 64, true><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::block64_attention_kernel<__half, 64, true><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
     else
-      piper::piper_attention_kernel<__half, 128, true><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::block64_attention_kernel<__half, 128, true><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
   } else {
     if (head_dim == 64)
-      piper::piper_attention_kernel<__nv_bfloat16, 64, true><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::block64_attention_kernel<__nv_bfloat16, 64, true><<<grid, piper::kAttnThreads, piper::AttnSmem<64>::kAlloc, s>>>(tmQ, tmK, tmV, p);
     else
-      piper::piper_attention_kernel<__nv_bfloat16, 128, true><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
+      piper::block64_attention_kernel<__nv_bfloat16, 128, true><<<grid, piper::kAttnThreads, piper::AttnSmem<128>::kAlloc, s>>>(tmQ, tmK, tmV, p);
   }
   PIPER_CUDA(cudaGetLastError());
   return PIPER_B200_OK;

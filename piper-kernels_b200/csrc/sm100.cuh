@@ -103,6 +103,45 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
   }
 }
 
+// Suspending probe: the thread may sleep in hardware until the phase
+// completes or about `hint_ns` pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for waits that are long by design (a tile waiting for the tensor
+// pipe while the other tile computes): the waiting warp sleeps in try_wait
+// instead of spinning, so it does not take issue slots from the warps that
+// share its SMSP.  Bounded in the same way.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, uint64_t budget_ns, uint32_t* status,
+                                                uint32_t status_bit, uint32_t abort_addr) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try(bar, parity, 1000u)) return true;
+    if (abort_addr != 0 && flag_get(abort_addr) != 0) return false;
+    if (global_timer_ns() - start > budget_ns) {
+      if (status != nullptr) atomicOr(status, status_bit);
+      if (abort_addr != 0) flag_set(abort_addr, 1u);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep_warp(uint32_t bar, uint32_t parity, uint64_t budget_ns,
+                                                     uint32_t* status, uint32_t status_bit, uint32_t abort_addr) {
+  const bool ok = mbar_wait_sleep(bar, parity, budget_ns, status, status_bit, abort_addr);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // Warp-uniform variant for code that synchronises the warp afterwards: every
 // lane waits (each bounded), then the warp agrees on success, so no lane can
 // leave a loop that its siblings stay in.

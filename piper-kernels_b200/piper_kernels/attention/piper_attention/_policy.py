@@ -12,13 +12,15 @@ do (``tests/attention/piper_attention/test_policy.py:18-21``).
 Fields (see ``piper_b200_plan_t``):
 
 * ``tile_rows``, ``key_block``, ``stages`` -- fixed by the compiled kernels
-  (two 128-row query tiles per CTA, 64-key softmax blocks, the K/V
-  shared-memory ring depth); reported, not chosen;
-* ``rearm`` -- kernel instance: re-arm the INT32 score accumulators with the
-  float bias pattern after each read and pass the probabilities to the PV
-  MMA through shared memory, or let the first QK^T step overwrite them, add
-  the bias in registers and write the probabilities into TMEM over the spent
-  scores, where the PV MMA reads them;
+  (two 128-row query tiles per CTA, 64-key softmax blocks, the depth of the
+  production kernel's K/V shared-memory ring in 128-key iterations);
+  reported, not chosen;
+* ``rearm`` -- kernel: ``False`` is the production kernel (128 keys, two
+  softmax blocks, per iteration with N = 128 QK^T MMAs; the bias added in
+  registers; the probabilities written into TMEM over the spent scores, where
+  the PV MMA reads them); ``True`` is the 64-key-block kernel that re-arms
+  the INT32 score accumulators with the float bias pattern after each read
+  and passes the probabilities to the PV MMA through shared memory;
 * ``heavy_first`` -- causal launches schedule the query tiles with the most
   visible keys first;
 * ``split_k`` / ``tail_tiles`` -- the split-KV tail: the trailing tiles of a

@@ -1,10 +1,10 @@
 """Execution-plan overrides and the offline tuner on the GPU (B200 only).
 
 Every plan the tuner can try must compute the same attention: each candidate
-(S re-arm instance, causal tile order, split-KV tail with 2..8 key ranges
-over various tail sizes) is launched on the same prepared operands and
-compared with the production plan (fp32 re-association of the split merge
-only) and with the oracle (the reference's GPU bounds).  Plans the kernels
+(production or re-arm kernel, causal tile order, split-KV tail with 2..8 key
+ranges over various tail sizes) is launched on the same prepared operands and
+compared with the production plan (rounding-level differences only) and with
+the oracle (the reference's GPU bounds).  Plans the kernels
 cannot run are refused by the library before any launch.
 """
 
@@ -60,8 +60,13 @@ def test_every_candidate_plan_computes_the_same_attention(shape, dtype, causal) 
     for plan, out in outs:
         err = (out.float() - base.float()).abs()
         assert err.max().item() < 0.02 and err.mean().item() < 2e-4, (plan, err.max().item())
-        if (plan.split_k, plan.tail_tiles) == (production.split_k, production.tail_tiles):
-            # The S instance and the tile order change no arithmetic.
+        if (plan.split_k, plan.tail_tiles, plan.rearm) == (production.split_k, production.tail_tiles,
+                                                            production.rearm):
+            # The tile order changes no arithmetic.  (The re-arm kernel takes
+            # its lazy-rescale decision per 64-key block, the production
+            # kernel per 128-key iteration: the same codes, but a rescale may
+            # land before or after a block's PV product, which moves fp32 and
+            # fp16 roundings; the bounds above cover that.)
             assert torch.equal(out, base), plan
         ref_err = (out.float().cpu() - expected).abs()
         assert ref_err.mean().item() < 0.003 and ref_err.max().item() < 0.12, plan
@@ -74,7 +79,7 @@ def test_plans_the_kernels_cannot_run_are_refused() -> None:
         prepared = prepare_piper_attention(q, k, v, True)
         production = default_execution_plan(prepared)
         with pytest.raises(ValueError, match="fixed by the kernels"):
-            launch_piper_attention(prepared, 0.125, plan=production.__class__(**{**production.as_dict(), "stages": 3}))
+            launch_piper_attention(prepared, 0.125, plan=production.__class__(**{**production.as_dict(), "stages": production.stages + 1}))
         with pytest.raises(ValueError, match="non-causal launches only"):
             launch_piper_attention(prepared, 0.125, plan=production.with_choices(split_k=2, tail_tiles=1))
 
