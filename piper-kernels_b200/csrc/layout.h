@@ -38,7 +38,7 @@ constexpr int kQueryGroup = 32;     // rows per Q scale (per_warp granularity)
 constexpr int kKeyGroup = 64;       // rows per K scale
 constexpr int kKeyBlock = 64;       // keys per online-softmax block (PV block)
 constexpr int kSumChunkRows = 512;  // rows per partial-sum chunk of the mean pass
-constexpr int kMaxSplitUnits = 256;  // split-KV tail CTAs (at most one wave on <= 256 SMs)
+constexpr int kMaxSplitUnits = 512;  // split-KV tail CTAs (a few waves of short units)
 constexpr int kMaxSplits = 8;       // key ranges per tail tile
 
 inline uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }

@@ -283,16 +283,19 @@ int run_prepass(const void* query, const int64_t query_strides[3], const void* k
 // Production plan of one attention launch over `q_rows` query rows and `keys`
 // keys per head (pure host logic).  The tile shape and ring depth are fixed by
 // the compiled kernels; the rest are the measured choices:
-//   - rearm = 0: the instance that adds the score bias in registers and keeps
-//     the probabilities in TMEM is faster for every launch kind (measured
-//     against the re-arm instance with shared-memory probabilities: c4 +4%,
-//     causal c3 +4%, D=64 +11%).
+//   - rearm = 0: the production kernel (128 keys per iteration, the
+//     probabilities in TMEM) is faster than the 64-key re-arm kernel for
+//     every launch kind.
 //   - heavy_first: causal grids run longest-work-first across all heads.
 //   - split-KV tail: when the tiles do not fill whole waves on the SMs, the
-//     `tail` tiles of the last partial wave are cut into
-//     k = min(kMaxSplits, SMs / tail, key blocks / 2) key ranges, so that the
-//     last wave ends sooner (non-causal launches, and only when the workspace
-//     has the split region).
+//     `tail` tiles of the last partial wave are cut into k key ranges, k in
+//     [2, min(kMaxSplits, key blocks / 2)] chosen to minimise the tail's time
+//     in tile units, ceil(tail * k / SMs) / k (the smaller k on ties); no
+//     split when no k beats one whole wave (non-causal launches, and only
+//     when the workspace has the split region for tail * k units).  For
+//     example 44 tail tiles on 148 SMs take k = 3 (one wave of third
+//     tiles), 96 take k = 3 (two waves of third tiles: 0.67 of a tile
+//     instead of a whole one).
 piper_b200_plan_t make_plan(int64_t bh, int64_t q_rows, int64_t keys, int64_t d, bool causal, int sms,
                             bool split_region, int64_t split_units_max) {
   piper_b200_plan_t P{};
@@ -306,9 +309,18 @@ piper_b200_plan_t make_plan(int64_t bh, int64_t q_rows, int64_t keys, int64_t d,
   if (!causal && split_region && P.tiles < (int64_t(1) << 30)) {
     const int64_t tail = P.tiles % sms;
     const int64_t blocks = (keys + piper::kKeyBlock - 1) / piper::kKeyBlock;
-    const int64_t k = tail > 0 ? std::min<int64_t>({int64_t(piper::kMaxSplits), sms / tail, blocks / 2}) : 0;
-    if (k >= 2 && tail * k <= split_units_max) {
-      P.split_k = static_cast<int32_t>(k);
+    // Compare costs as fractions ceil(tail*k/sms)/k against best_num/best_den.
+    int64_t best_k = 0, best_num = 1, best_den = 1;
+    for (int64_t k = 2; tail > 0 && k <= piper::kMaxSplits && k <= blocks / 2 && tail * k <= split_units_max; ++k) {
+      const int64_t waves = (tail * k + sms - 1) / sms;
+      if (waves * best_den < best_num * k) {
+        best_k = k;
+        best_num = waves;
+        best_den = k;
+      }
+    }
+    if (best_k > 0) {
+      P.split_k = static_cast<int32_t>(best_k);
       P.tail_tiles = tail;
     }
   }

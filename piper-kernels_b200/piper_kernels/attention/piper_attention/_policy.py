@@ -40,7 +40,7 @@ from ..._targets import AcceleratorTarget
 B200_SMS = 148
 # Split-KV CTAs the workspace's split region holds at most (kMaxSplitUnits in
 # the library's layout): tail_tiles * split_k may not exceed it.
-SPLIT_UNITS_MAX = 256
+SPLIT_UNITS_MAX = 512
 
 
 @dataclass(frozen=True, slots=True)

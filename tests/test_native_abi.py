@@ -48,7 +48,7 @@ def test_workspace_layout_regions_are_aligned_and_disjoint() -> None:
             (L.split_state, L.split_units_max * 256 * (d + 2) * 4),
         ]
         tiles = bh * -(-nq // 256)
-        assert L.split_units_max == min(256, 8 * tiles)
+        assert L.split_units_max == min(512, 8 * tiles)
         # The K/V pack is the contiguous span from the K codes to the end of vrcp.
         assert L.kv_pack == L.k8
         assert L.vrcp + bh * L.nk_pad * 4 <= L.kv_pack + L.kv_pack_bytes <= L.kmean

@@ -12,7 +12,11 @@ from __future__ import annotations
 import pytest
 
 from piper_kernels._targets import AcceleratorTarget
-from piper_kernels.attention.piper_attention._policy import PiperAttentionExecutionPlan, select_execution_plan
+from piper_kernels.attention.piper_attention._policy import (
+    SPLIT_UNITS_MAX,
+    PiperAttentionExecutionPlan,
+    select_execution_plan,
+)
 
 B200 = AcceleratorTarget("cuda", "sm100", 148)
 SMALL = AcceleratorTarget("cuda", "sm100", 132)
@@ -34,7 +38,7 @@ def test_c4_plan_on_a_b200() -> None:
     plan = _select()
     # 40 heads x 64 tiles = 2560 tiles = 17 waves + 44 tiles on 148 SMs.
     assert plan.tiles == 2560 and plan.sms == 148
-    assert plan.tail_tiles == 44 and plan.split_k == 3  # min(8, 148 // 44, 256 // 2)
+    assert plan.tail_tiles == 44 and plan.split_k == 3  # one wave of 132 third-tiles
     assert plan.ctas == 2560 - 44 + 44 * 3 and plan.kernels == 2
     assert not plan.rearm and not plan.heavy_first
 
@@ -43,6 +47,28 @@ def test_five_heads_per_gpu_fill_the_last_wave() -> None:
     # c4 split over 8 GPUs: 320 tiles = 2 waves + 24 tiles, each cut into 6 key ranges.
     plan = _select(heads=5)
     assert plan.tail_tiles == 24 and plan.split_k == 6 and plan.ctas == 296 + 144
+
+
+def test_twenty_heads_per_gpu_split_into_two_waves_of_thirds() -> None:
+    # c4 split over 2 GPUs: 1280 tiles = 8 waves + 96 tiles.  No k <= 148 / 96
+    # helps, but k = 3 gives 288 third-tiles in two waves: 0.67 of a tile
+    # instead of a whole wave.
+    plan = _select(heads=20)
+    assert plan.tail_tiles == 96 and plan.split_k == 3 and plan.ctas == 1184 + 288
+
+
+def test_split_minimises_the_tail_in_tile_units() -> None:
+    from math import ceil
+    for heads in range(1, 80):
+        plan = _select(heads=heads)
+        tail = plan.tiles % 148
+        cost = (lambda k: ceil(tail * k / 148) / k)
+        best = min([1.0] + [cost(k) for k in range(2, 9) if tail * k <= SPLIT_UNITS_MAX])
+        if plan.split_k == 0:
+            assert tail == 0 or best == 1.0
+        else:
+            assert plan.tail_tiles == tail and abs(cost(plan.split_k) - best) < 1e-12
+            assert all(cost(k) > best for k in range(2, plan.split_k))  # the smallest best k
 
 
 def test_split_depends_on_the_sm_count() -> None:

@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from piper_kernels._targets import AcceleratorTarget
-from piper_kernels.attention.piper_attention._policy import select_execution_plan
+from piper_kernels.attention.piper_attention._policy import SPLIT_UNITS_MAX, select_execution_plan
 from piper_kernels.benchmarking import Timing, measure_quality
 from piper_kernels.tuning import (
     MEASURED,
@@ -54,7 +54,7 @@ def test_split_candidates_on_an_unsplit_production_cut_the_last_partial_wave() -
     prod = _production(heads=37, n=1024)  # 148 tiles: whole waves, no split
     assert prod.split_k == 0
     (split,) = [p for p in candidate_plans(prod, split_k=[0, 4]) if p.split_k]
-    assert split.tail_tiles == 256 // 4 and split.kernels == 2  # capped by the split region
+    assert split.tail_tiles == min(148, SPLIT_UNITS_MAX // 4) and split.kernels == 2  # capped by the split region
 
 
 def test_too_many_candidates_is_an_error() -> None:
