@@ -1091,62 +1091,62 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // Combines the partial states of the split tail tiles: with M = max_i m_i,
 // out = sum_i O_i 2^(m_i - M) / max(sum_i l_i 2^(m_i - M), 1e-30) + mean_V
 // (the same identity as the lazy rescale), or under kStateStore the merged
-// state (sum_i O_i 2^(m_i - M), M, sum_i l_i 2^(m_i - M)).  grid (tail
-// tiles), 256 threads: one query row each.
+// state (sum_i O_i 2^(m_i - M), M, sum_i l_i 2^(m_i - M)).  One thread per
+// (query row, 8 columns): grid (tail tiles, D / 8), 256 threads = 256 / (D /
+// 8) rows x D / 8 column chunks, so even a handful of tail tiles spreads over
+// many SMs (one CTA per tile, a row per thread, kept 24 SMs busy for the 24
+// tail tiles of a 5-head launch).
 template <typename T, int D>
 __global__ void __launch_bounds__(kTileM * kTiles) merge_split_kernel(const AttnParams p) {
+  constexpr int kChunks = D / 8;                      // 8-column chunks per row
+  constexpr int kRowsPerCta = kTileM * kTiles / kChunks;
+  constexpr int kRows = kTileM * kTiles;
   const int64_t st = blockIdx.x;
   const int64_t tile = p.main_units + st;
   int64_t bh;
   int qt;
   tile_coords(p, tile, bh, qt);  // same tile order as the attention kernel
-  const int64_t row = static_cast<int64_t>(qt) * (kTileM * kTiles) + threadIdx.x;
+  const int r = static_cast<int>(blockIdx.y) * kRowsPerCta + static_cast<int>(threadIdx.x) / kChunks;  // row in the tile
+  const int c = static_cast<int>(threadIdx.x) % kChunks;
+  const int64_t row = static_cast<int64_t>(qt) * kRows + r;
   if (row >= p.nq) return;
-  constexpr int kRows = kTileM * kTiles;
   const float2* ml = reinterpret_cast<const float2*>(p.split_state + p.split_units * kRows * D);
   float mx = -INFINITY;
-  for (int i = 0; i < p.splits; ++i) mx = fmaxf(mx, ml[(st * p.splits + i) * kRows + threadIdx.x].x);
+  for (int i = 0; i < p.splits; ++i) mx = fmaxf(mx, ml[(st * p.splits + i) * kRows + r].x);
   float l = 0.0f;
-  float w[kMaxSplits];
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int i = 0; i < p.splits; ++i) {
-    const float2 v = ml[(st * p.splits + i) * kRows + threadIdx.x];
-    w[i] = ex2_approx(v.x - mx);
-    l = fmaf(v.y, w[i], l);
+    const float2 v = ml[(st * p.splits + i) * kRows + r];
+    const float w = ex2_approx(v.x - mx);
+    l = fmaf(v.y, w, l);
+    const float4* so = reinterpret_cast<const float4*>(p.split_state + ((st * p.splits + i) * kRows + r) * D) + 2 * c;
+    const float4 a = so[0], b = so[1];
+    acc[0] = fmaf(a.x, w, acc[0]);
+    acc[1] = fmaf(a.y, w, acc[1]);
+    acc[2] = fmaf(a.z, w, acc[2]);
+    acc[3] = fmaf(a.w, w, acc[3]);
+    acc[4] = fmaf(b.x, w, acc[4]);
+    acc[5] = fmaf(b.y, w, acc[5]);
+    acc[6] = fmaf(b.z, w, acc[6]);
+    acc[7] = fmaf(b.w, w, acc[7]);
   }
-  const bool store = (p.state_mode & kStateStore) != 0;
-  const float inv = 1.0f / fmaxf(l, 1e-30f);
-  const float* vm = p.vmean + bh * D;
   const int64_t grow = p.q_row0 + row;
-  uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + grow) * D);
-  float4* srow = reinterpret_cast<float4*>(p.state_o + (bh * p.nq_all + grow) * D);
-#pragma unroll 4
-  for (int c = 0; c < D / 8; ++c) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int i = 0; i < p.splits; ++i) {
-      const float4* so = reinterpret_cast<const float4*>(p.split_state + ((st * p.splits + i) * kRows + threadIdx.x) * D);
-      const float4 a = so[2 * c], b = so[2 * c + 1];
-      acc[0] = fmaf(a.x, w[i], acc[0]);
-      acc[1] = fmaf(a.y, w[i], acc[1]);
-      acc[2] = fmaf(a.z, w[i], acc[2]);
-      acc[3] = fmaf(a.w, w[i], acc[3]);
-      acc[4] = fmaf(b.x, w[i], acc[4]);
-      acc[5] = fmaf(b.y, w[i], acc[5]);
-      acc[6] = fmaf(b.z, w[i], acc[6]);
-      acc[7] = fmaf(b.w, w[i], acc[7]);
-    }
-    if (store) {
-      srow[2 * c] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      srow[2 * c + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    } else {
-      uint4 pk;
-      pk.x = pack2<T>(fmaf(acc[0], inv, vm[8 * c]), fmaf(acc[1], inv, vm[8 * c + 1]));
-      pk.y = pack2<T>(fmaf(acc[2], inv, vm[8 * c + 2]), fmaf(acc[3], inv, vm[8 * c + 3]));
-      pk.z = pack2<T>(fmaf(acc[4], inv, vm[8 * c + 4]), fmaf(acc[5], inv, vm[8 * c + 5]));
-      pk.w = pack2<T>(fmaf(acc[6], inv, vm[8 * c + 6]), fmaf(acc[7], inv, vm[8 * c + 7]));
-      orow[c] = pk;
-    }
+  if (p.state_mode & kStateStore) {
+    float4* srow = reinterpret_cast<float4*>(p.state_o + (bh * p.nq_all + grow) * D) + 2 * c;
+    srow[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    srow[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    if (c == 0) reinterpret_cast<float2*>(p.state_ml)[bh * p.nq_all + grow] = make_float2(mx, l);
+  } else {
+    const float inv = 1.0f / fmaxf(l, 1e-30f);
+    const float4* vm = reinterpret_cast<const float4*>(p.vmean + bh * D) + 2 * c;
+    const float4 m0 = vm[0], m1 = vm[1];
+    uint4 pk;
+    pk.x = pack2<T>(fmaf(acc[0], inv, m0.x), fmaf(acc[1], inv, m0.y));
+    pk.y = pack2<T>(fmaf(acc[2], inv, m0.z), fmaf(acc[3], inv, m0.w));
+    pk.z = pack2<T>(fmaf(acc[4], inv, m1.x), fmaf(acc[5], inv, m1.y));
+    pk.w = pack2<T>(fmaf(acc[6], inv, m1.z), fmaf(acc[7], inv, m1.w));
+    reinterpret_cast<uint4*>(static_cast<T*>(p.out) + (bh * p.nq_all + grow) * D)[c] = pk;
   }
-  if (store) reinterpret_cast<float2*>(p.state_ml)[bh * p.nq_all + grow] = make_float2(mx, l);
 }
 
 // ---------------------------------------------------------------------------

@@ -477,7 +477,8 @@ int run_attention(void* out, int dtype, int64_t batch, int64_t heads, int64_t nq
   const dim3 grid = units < (int64_t(1) << 31) ? dim3(static_cast<unsigned>(units), 1)
                                                 : dim3(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(bh));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 merge_grid(static_cast<unsigned>(p.split_units > 0 ? p.split_units / p.splits : 0));
+  const dim3 merge_grid(static_cast<unsigned>(p.split_units > 0 ? p.split_units / p.splits : 0),
+                        static_cast<unsigned>(head_dim / 8));
   if (dtype == PIPER_B200_FLOAT16) {
     if (head_dim == 64)
       launch_piper_kernels<__half, 64>(grid, merge_grid, plan.rearm != 0, tmQ, tmK, tmV, p, s);
