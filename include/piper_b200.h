@@ -138,7 +138,7 @@ typedef struct piper_b200_plan_s {
   int32_t stages;      /* depth of the production kernel's K/V shared-memory ring, in iterations
                           of 128 keys */
   int32_t rearm;       /* 0: the production kernel: 128 keys (two blocks) per iteration with
-                          N = 128 QK^T MMAs, the bias added in registers and the probabilities
+                          N = 128 QK^T MMAs, the scores converted with I2F and the probabilities
                           written into TMEM over the spent scores;
                           1: the 64-key-block kernel that re-arms the S accumulators with the
                           bias pattern after each read and passes the probabilities through

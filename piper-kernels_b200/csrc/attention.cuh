@@ -480,25 +480,30 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
 }
 
 // x = S*c + log2(vs_k) for the 64 scores of a block (two packed f32 per
-// pair of keys).  The INT32 scores read as floats 1.5*2^23 + S either because
-// the accumulator was pre-biased (kAddBias false) or because the bias bits
-// are added here as integers to a score accumulated from zero (kAddBias
-// true); one packed subtraction then leaves S exactly.
-template <bool kAddBias>
+// pair of keys).  kFromZero false: the accumulator was pre-biased, so the
+// INT32 scores read as floats 1.5*2^23 + S and one packed subtraction leaves
+// S exactly.  kFromZero true: the scores were accumulated from zero and are
+// converted with I2F, also exactly (|S| < 2^22); measured on the 128-key
+// kernel against adding the bias bits as integers and subtracting: c4 +6.8%,
+// c2 +5.5%, causal c3 +5.8%, D = 64 +9.4%, identical results.
+template <bool kFromZero>
 __device__ __forceinline__ void scores_to_x(const uint32_t (&a)[32], const uint32_t (&b)[32], float2 (&x)[32],
                                             float c, uint32_t vl) {
-  const uint32_t add = kAddBias ? kBiasBits : 0u;
   const float2 c2 = make_float2(c, c);
   const float2 nb2 = make_float2(-kBias, -kBias);
+  auto pair = [&](uint32_t u0, uint32_t u1) {
+    if constexpr (kFromZero)
+      return make_float2(__int2float_rn(static_cast<int>(u0)), __int2float_rn(static_cast<int>(u1)));
+    else
+      return __fadd2_rn(f2(u0, u1), nb2);
+  };
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float4 la = lds128(vl + 16 * i), lb = lds128(vl + 16 * (8 + i));
-    x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i] + add, a[4 * i + 1] + add), nb2), c2, make_float2(la.x, la.y));
-    x[2 * i + 1] =
-        __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2] + add, a[4 * i + 3] + add), nb2), c2, make_float2(la.z, la.w));
-    x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i] + add, b[4 * i + 1] + add), nb2), c2, make_float2(lb.x, lb.y));
-    x[16 + 2 * i + 1] =
-        __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2] + add, b[4 * i + 3] + add), nb2), c2, make_float2(lb.z, lb.w));
+    x[2 * i] = __ffma2_rn(pair(a[4 * i], a[4 * i + 1]), c2, make_float2(la.x, la.y));
+    x[2 * i + 1] = __ffma2_rn(pair(a[4 * i + 2], a[4 * i + 3]), c2, make_float2(la.z, la.w));
+    x[16 + 2 * i] = __ffma2_rn(pair(b[4 * i], b[4 * i + 1]), c2, make_float2(lb.x, lb.y));
+    x[16 + 2 * i + 1] = __ffma2_rn(pair(b[4 * i + 2], b[4 * i + 3]), c2, make_float2(lb.z, lb.w));
   }
 }
 

@@ -16,8 +16,8 @@ Fields (see ``piper_b200_plan_t``):
   production kernel's K/V shared-memory ring in 128-key iterations);
   reported, not chosen;
 * ``rearm`` -- kernel: ``False`` is the production kernel (128 keys, two
-  softmax blocks, per iteration with N = 128 QK^T MMAs; the bias added in
-  registers; the probabilities written into TMEM over the spent scores, where
+  softmax blocks, per iteration with N = 128 QK^T MMAs; the INT32 scores
+  converted with I2F; the probabilities written into TMEM over the spent scores, where
   the PV MMA reads them); ``True`` is the 64-key-block kernel that re-arms
   the INT32 score accumulators with the float bias pattern after each read
   and passes the probabilities to the PV MMA through shared memory;
