@@ -166,10 +166,11 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The TMEM score accumulators are pre-loaded with the bit pattern of 1.5*2^23
-// before every QK^T chain (which accumulates onto it), so an INT32 result v
-// with |v| < 2^22 reads back as the float 1.5*2^23 + v exactly: one packed
-// subtraction converts two values.
+// In the re-arm form the TMEM score accumulators are pre-loaded with the bit
+// pattern of 1.5*2^23 before every QK^T chain (which accumulates onto it), so
+// an INT32 result v with |v| < 2^22 reads back as the float 1.5*2^23 + v
+// exactly: one packed subtraction converts two values.  The other kernels
+// accumulate S from zero and convert with I2F.
 constexpr uint32_t kBiasBits = 0x4B400000u;
 constexpr float kBias = 12582912.0f;
 constexpr float kLog2FP8Max = 8.807354922057604f;  // log2(448): SageAttention2++ P codes top out at 448
@@ -210,6 +211,11 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
+}
+
+// Two INT32 scores accumulated from zero as floats (exact: |S| < 2^22).
+__device__ __forceinline__ float2 i2f_pair(uint32_t u0, uint32_t u1) {
+  return make_float2(__int2float_rn(static_cast<int>(u0)), __int2float_rn(static_cast<int>(u1)));
 }
 
 // Writes the bias pattern into `cols` consecutive TMEM columns of this lane.
@@ -329,7 +335,6 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
   const float qs = valid_row ? __ldg(p.qscale + bh * p.nq_all + p.q_row0 + row) : 0.0f;
   const float c_row = qs * p.scale_log2e;
   const float2 c2 = make_float2(c_row, c_row);
-  const float2 nb2 = make_float2(-kBias, -kBias);
   float m_run = -INFINITY, l_run = 0.0f;
   bool ok = true;
   int pv_seen = 0;  // pv_full completions consumed (one per block)
@@ -349,21 +354,20 @@ __device__ __forceinline__ void sage_softmax_role(const AttnParams& p, uint8_t* 
       tmem_ld32_split(tm_s + buf * kKeyBlock, a);
       tmem_ld32_split(tm_s + buf * kKeyBlock + 32, b);
       tmem_ld_wait();
-      tmem_fill_bias<kKeyBlock>(tm_s + buf * kKeyBlock);
       const uint32_t vm = sbase + S::kOffVec + s * S::kVecBytes;  // padded-key mask
       const uint32_t vk = vm + kKeyBlock * 4;                     // per-key K scale
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 ma = lds128(vm + 16 * i), mb = lds128(vm + 16 * (8 + i));
         const float4 ka = lds128(vk + 16 * i), kb = lds128(vk + 16 * (8 + i));
-        x[2 * i] = __ffma2_rn(__fadd2_rn(f2(a[4 * i], a[4 * i + 1]), nb2), __fmul2_rn(c2, make_float2(ka.x, ka.y)),
+        x[2 * i] = __ffma2_rn(i2f_pair(a[4 * i], a[4 * i + 1]), __fmul2_rn(c2, make_float2(ka.x, ka.y)),
                               make_float2(ma.x, ma.y));
-        x[2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(a[4 * i + 2], a[4 * i + 3]), nb2),
-                                  __fmul2_rn(c2, make_float2(ka.z, ka.w)), make_float2(ma.z, ma.w));
-        x[16 + 2 * i] = __ffma2_rn(__fadd2_rn(f2(b[4 * i], b[4 * i + 1]), nb2),
-                                   __fmul2_rn(c2, make_float2(kb.x, kb.y)), make_float2(mb.x, mb.y));
-        x[16 + 2 * i + 1] = __ffma2_rn(__fadd2_rn(f2(b[4 * i + 2], b[4 * i + 3]), nb2),
-                                       __fmul2_rn(c2, make_float2(kb.z, kb.w)), make_float2(mb.z, mb.w));
+        x[2 * i + 1] = __ffma2_rn(i2f_pair(a[4 * i + 2], a[4 * i + 3]), __fmul2_rn(c2, make_float2(ka.z, ka.w)),
+                                  make_float2(ma.z, ma.w));
+        x[16 + 2 * i] = __ffma2_rn(i2f_pair(b[4 * i], b[4 * i + 1]), __fmul2_rn(c2, make_float2(kb.x, kb.y)),
+                                   make_float2(mb.x, mb.y));
+        x[16 + 2 * i + 1] = __ffma2_rn(i2f_pair(b[4 * i + 2], b[4 * i + 3]), __fmul2_rn(c2, make_float2(kb.z, kb.w)),
+                                       make_float2(mb.z, mb.w));
       }
     }
     if (p.causal) {
@@ -493,7 +497,7 @@ __device__ __forceinline__ void scores_to_x(const uint32_t (&a)[32], const uint3
   const float2 nb2 = make_float2(-kBias, -kBias);
   auto pair = [&](uint32_t u0, uint32_t u1) {
     if constexpr (kFromZero)
-      return make_float2(__int2float_rn(static_cast<int>(u0)), __int2float_rn(static_cast<int>(u1)));
+      return i2f_pair(u0, u1);
     else
       return __fadd2_rn(f2(u0, u1), nb2);
   };
@@ -930,10 +934,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint64_t budget = p.wait_budget_ns;
   uint32_t* status = &g_piper_status;
   if (warp < 8) {
-    // Every QK^T MMA accumulates onto the bias pattern: arm both S buffers of
-    // this thread's lane, and clear its numerator, before the first MMA.
+    // Re-arm form: every QK^T MMA accumulates onto the bias pattern, so both
+    // S buffers of this thread's lane are armed before the first MMA
+    // (SageAttention2++ accumulates S from zero).  The numerator is cleared.
     const uint32_t lane_tm = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16) + (warp / 4) * 256;
-    tmem_fill_bias<2 * kKeyBlock>(lane_tm);
+    if constexpr (!kSage) tmem_fill_bias<2 * kKeyBlock>(lane_tm);
     // The F32 numerator accumulates from zero.
 #pragma unroll
     for (int c = 0; c < D; c += 4) tmem_st4_same(lane_tm + 128 + c, 0u);
@@ -1016,7 +1021,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const uint32_t dcol = tmem_base + t * 256 + (jq & 1) * kKeyBlock;
 #pragma unroll
             for (int kk = 0; kk < D / 32; ++kk)
-              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, 1u);
+              umma_i8(dcol, descQ[t] + 2 * kk, descK + 2 * kk, kIdescQK, (kSage && kk == 0) ? 0u : 1u);
             umma_commit(s_full + 8 * (t * 2 + (jq & 1)));
             qk_next[t] = jq + 1;
             progress = true;
