@@ -207,12 +207,6 @@ __device__ __forceinline__ float2 f2(uint32_t a, uint32_t b) {
   return make_float2(__uint_as_float(a), __uint_as_float(b));
 }
 
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 // Two INT32 scores accumulated from zero as floats (exact: |S| < 2^22).
 __device__ __forceinline__ float2 i2f_pair(uint32_t u0, uint32_t u1) {
   return make_float2(__int2float_rn(static_cast<int>(u0)), __int2float_rn(static_cast<int>(u1)));

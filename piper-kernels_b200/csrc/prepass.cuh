@@ -31,6 +31,7 @@
 #include <math.h>
 
 #include "layout.h"
+#include "sm100.cuh"
 
 namespace piper {
 
@@ -107,9 +108,10 @@ __device__ __forceinline__ void unpack8(const uint4& r, float (&out)[8]) {
 // ---------------------------------------------------------------------------
 // Column sums of K (and V when non-causal) over one chunk of rows, in fp64.
 template <typename T, int D, bool kVec16>
-// Three CTAs per SM keep more loads in flight (measured: the prepass is
-// latency-bound at two).
-__global__ void __launch_bounds__(kPrepassThreads, 3) kv_sum_kernel(PrepassArgs a) {
+// Eight rows per step (16 loads of 16 bytes in flight per thread with V) at
+// two CTAs per SM: measured 5% faster on c4 than four rows per step at three
+// CTAs per SM, and than a software-pipelined form at two.
+__global__ void __launch_bounds__(kPrepassThreads, 2) kv_sum_kernel(PrepassArgs a) {
   constexpr int kVpr = D / 8;                      // 16-byte vectors per row
   constexpr int kRpp = kPrepassThreads / kVpr;     // rows per pass
   __shared__ double red[2][kRpp][D];
@@ -131,9 +133,9 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) kv_sum_kernel(PrepassArgs 
 
   const int64_t r0 = static_cast<int64_t>(chunk) * kSumChunkRows;
   const int64_t r1 = min(r0 + kSumChunkRows, a.nk);
-  // Four rows per step with all their loads issued first, so each thread
-  // keeps 4 (K only) or 8 (K and V) 16-byte loads in flight.
-  constexpr int kUnroll = 4;
+  // kUnroll rows per step with all their loads issued first, so each thread
+  // keeps kUnroll (K only) or 2 kUnroll (K and V) 16-byte loads in flight.
+  constexpr int kUnroll = 8;
   int64_t r = r0 + ro;
   for (; r + (kUnroll - 1) * kRpp < r1; r += kUnroll * kRpp) {
     uint4 rk[kUnroll], rv[kUnroll];
@@ -236,70 +238,109 @@ __global__ void __launch_bounds__(D) finalize_means_kernel(PrepassArgs a) {
   vmean[bh * D + tid] = a.causal ? 0.0f : static_cast<float>(totals[(bh_all + bh) * D + tid] / n);
 }
 
-// Eight INT8 codes packed into two words, computed in packed f32x2
-// arithmetic.  The near-tie test of all eight feeds one vote over the active
-// lanes, so the exact-division fallback is a real branch that warps skip
-// unless one of their lanes has a near-tie (it is never issued predicated
-// off for every element).
-__device__ __forceinline__ uint2 pack_codes(const float (&x)[8], float s, float rs) {
-  uint32_t y[8];
-  bool near = false;
+// Eight INT8 codes as the bits of q + 1.5*2^23 (the code is the low byte),
+// computed in packed f32x2 arithmetic.  One near-tie test covers all eight,
+// through their largest distance from the rounded value, and feeds one vote
+// over the active lanes, so the exact-division fallback is a real branch
+// that warps skip unless one of their lanes has a near-tie (it is never
+// issued predicated off for every element).
+__device__ __forceinline__ void round_codes(const float (&x)[8], float s, float rs, uint32_t (&y)[8]) {
+  float dm = 0.0f;
 #pragma unroll
   for (int i = 0; i < 8; i += 2) {
     const float2 q = __fmul2_rn(make_float2(x[i], x[i + 1]), make_float2(rs, rs));
     const float2 t = __fadd2_rn(q, make_float2(kMagic, kMagic));
     const float2 r = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
     const float2 d = __ffma2_rn(r, make_float2(-1.0f, -1.0f), q);
-    near |= (fabsf(d.x) > kNearTie) | (fabsf(d.y) > kNearTie);
+    dm = fmax3(dm, fabsf(d.x), fabsf(d.y));
     y[i] = __float_as_uint(t.x);
     y[i + 1] = __float_as_uint(t.y);
   }
-  if (__any_sync(__activemask(), near)) {
+  if (__any_sync(__activemask(), dm > kNearTie)) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float q = __fmul_rn(x[i], rs);
       if (fabsf(__fsub_rn(q, __fsub_rn(__fadd_rn(q, kMagic), kMagic))) > kNearTie) y[i] = exact_code_bits(x[i], s);
     }
   }
+}
+
+// Eight INT8 codes packed into two words.
+__device__ __forceinline__ uint2 pack_codes(const float (&x)[8], float s, float rs) {
+  uint32_t y[8];
+  round_codes(x, s, rs, y);
   const uint32_t w0 = __byte_perm(__byte_perm(y[0], y[1], 0x0040), __byte_perm(y[2], y[3], 0x0040), 0x5410);
   const uint32_t w1 = __byte_perm(__byte_perm(y[4], y[5], 0x0040), __byte_perm(y[6], y[7], 0x0040), 0x5410);
   return make_uint2(w0, w1);
 }
 
-// One 64-row tile of Q, K and V per CTA.  All loads are issued up front; the
-// two 32-row Q group maxima and the 64-row K group max share one block-wide
-// reduction; each V row's max is a shuffle among the threads of that row.  V
-// codes go row-major into a padded shared tile (row stride D/4+1 words, so
-// rows fall on distinct banks), then are transposed 4x4 bytes at a time with
-// byte permutes and written as [D, keys] with coalesced 4-byte stores.
-// Four INT8 codes (one per byte) to four fp16 values, exactly: byte b holds
-// c; (c + 128) placed under the fp16 exponent of 1024 reads as 1152 + c, and
-// one packed subtraction leaves c.
-__device__ __forceinline__ uint2 codes_to_f16x4(uint32_t w) {
-  const uint32_t u = w ^ 0x80808080u;  // c + 128 in each byte
-  const __half2 k = __halves2half2(__float2half_rn(1152.0f), __float2half_rn(1152.0f));
-  uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140);  // halves 0x64:(c0+128), 0x64:(c1+128)
-  uint32_t hi = __byte_perm(u, 0x64646464u, 0x5342);
-  __half2 a = __hsub2(*reinterpret_cast<__half2*>(&lo), k);
-  __half2 b = __hsub2(*reinterpret_cast<__half2*>(&hi), k);
-  return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+// Eight INT8 codes as fp16 values (exact: integers in [-127, 127]), packed
+// in pairs: the V operand of the attention kernel's fp16 PV product.
+__device__ __forceinline__ uint4 pack_codes_f16(const float (&x)[8], float s, float rs) {
+  uint32_t y[8];
+  round_codes(x, s, rs, y);
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 c = __fadd2_rn(make_float2(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1])),
+                                make_float2(-kMagic, -kMagic));
+    const __half2 h = __floats2half2_rn(c.x, c.y);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <typename T, int D, bool kVec16>
-// Three CTAs per SM (80 registers, a few spilled) beat two at 111 registers
-// by about 10% on the whole prepass: more 16-byte loads in flight.
-__global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArgs a) {
+// Largest |x| of eight raw fp16/bf16 values (one 16-byte vector) and `acc`,
+// in packed 16-bit arithmetic: the maximum is exact in the input type, so it
+// converts to the same float as the fp32 maximum of the widened values.
+template <typename T>
+struct PairOf;
+template <>
+struct PairOf<__half> {
+  using type = __half2;
+};
+template <>
+struct PairOf<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t absmax8(const uint4& r, uint32_t acc) {
+  using P = typename PairOf<T>::type;
+  P m = *reinterpret_cast<const P*>(&acc);
+  const P* e = reinterpret_cast<const P*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m = __hmax2(m, __habs2(e[i]));
+  return *reinterpret_cast<const uint32_t*>(&m);
+}
+
+template <typename T>
+__device__ __forceinline__ float absmax_pair_to_f32(uint32_t m) {
+  const T* e = reinterpret_cast<const T*>(&m);
+  return fmaxf(to_f32<T>(e[0]), to_f32<T>(e[1]));
+}
+
+// The arithmetic of one 64-row tile of Q, K and V, given each thread's raw
+// 16-byte vectors (rows past a sequence end hold zeros).  The two 32-row Q
+// group maxima (packed 16-bit maxima of the raw values) and the 64-row K
+// group max share one block-wide reduction; each V row's max is a shuffle
+// among the threads of that row.  V codes go row-major as fp16 into a padded
+// shared tile (row stride D/2 + 1 words, so rows fall on distinct banks), then
+// are transposed 4 keys x 2 features at a time with two permutes and written
+// as [D, keys] with 8-byte stores.  Contains CTA-wide barriers: every thread
+// of the CTA calls it for the same tile.  `vrow` is the padded V code tile,
+// `red` the per-warp maxima.
+template <typename T, int D>
+__device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, int tile,
+                                              const uint4 (&rq)[kKeyBlock / (kPrepassThreads / (D / 8))],
+                                              const uint4 (&rk)[kKeyBlock / (kPrepassThreads / (D / 8))],
+                                              const uint4 (&rv)[kKeyBlock / (kPrepassThreads / (D / 8))],
+                                              uint32_t* vrow, float (*red)[3]) {
   constexpr int kVpr = D / 8;                   // 16-byte vectors per row
   constexpr int kRpp = kPrepassThreads / kVpr;  // rows per pass
   constexpr int kPasses = kKeyBlock / kRpp;     // passes over the 64-row tile
-  constexpr int kRowWords = D / 4 + 1;          // padded V code row, in words
+  constexpr int kRowWords = D / 2 + 1;          // padded fp16 V code row, in words
   constexpr int kWarps = kPrepassThreads / 32;
-  __shared__ float red[kWarps][3];
-  __shared__ uint32_t vrow[kKeyBlock * kRowWords];
-
-  const int tile = blockIdx.x;
-  const int64_t bh = blockIdx.y;
-  const int64_t b = bh / a.heads, h = bh % a.heads;
   const int tid = threadIdx.x;
   const int lane = tid % 32, warp = tid / 32;
   const int vec = tid % kVpr;
@@ -308,19 +349,6 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
   const auto& L = a.L;
   const bool has_q = row0 < a.nq;
   const bool has_kv = row0 < a.nk;
-
-  const T* qb = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + vec * 8;
-  const T* kb = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + vec * 8;
-  const T* vb = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + vec * 8;
-  uint4 rq[kPasses], rk[kPasses], rv[kPasses];
-#pragma unroll
-  for (int p = 0; p < kPasses; ++p) {
-    const int64_t r = row0 + ro + p * kRpp;
-    rq[p] = (r < a.nq) ? load_raw8<T, kVec16>(qb + r * a.qs[2]) : make_uint4(0u, 0u, 0u, 0u);
-    const bool kv_ok = r < a.nk;
-    rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + r * a.ks[2]) : make_uint4(0u, 0u, 0u, 0u);
-    rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + r * a.vs[2]) : make_uint4(0u, 0u, 0u, 0u);
-  }
   float km[8], vm[8];
   {
     const float* kmean = reinterpret_cast<const float*>(a.ws + L.kmean) + bh * D + vec * 8;
@@ -331,23 +359,38 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
       vm[i] = (has_kv && !a.causal) ? vmean[i] : 0.0f;
     }
   }
+  // Negated means in pairs: x - m is computed as x + (-m), the same IEEE result.
+  float2 nkm[4], nvm[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    nkm[i] = make_float2(-km[2 * i], -km[2 * i + 1]);
+    nvm[i] = make_float2(-vm[2 * i], -vm[2 * i + 1]);
+  }
 
   // ---- group maxima: Q (two 32-row groups) and centered K (one 64-row group);
   // rows past the sequence end count as zero, as the reference's zero padding.
-  float am[3] = {0.0f, 0.0f, 0.0f};
+  float am[3];
+  {
+    uint32_t qm[2] = {0u, 0u};  // packed |q| maxima of the two Q groups
+    float kmx = 0.0f;
 #pragma unroll
-  for (int p = 0; p < kPasses; ++p) {
-    const int64_t r = row0 + ro + p * kRpp;
-    float x[8];
-    unpack8<T>(rq[p], x);
-    const int g = (p * kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
+    for (int p = 0; p < kPasses; ++p) {
+      const int64_t r = row0 + ro + p * kRpp;
+      const int g = (p * kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
+      qm[g] = absmax8<T>(rq[p], qm[g]);
+      if (r < a.nk) {
+        float x[8];
+        unpack8<T>(rk[p], x);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) am[g] = fmaxf(am[g], fabsf(x[i]));
-    if (r < a.nk) {
-      unpack8<T>(rk[p], x);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) am[2] = fmaxf(am[2], fabsf(__fsub_rn(x[i], km[i])));
+        for (int i = 0; i < 4; ++i) {
+          const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nkm[i]);
+          kmx = fmax3(kmx, fabsf(c.x), fabsf(c.y));
+        }
+      }
     }
+    am[0] = absmax_pair_to_f32<T>(qm[0]);
+    am[1] = absmax_pair_to_f32<T>(qm[1]);
+    am[2] = kmx;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -402,13 +445,18 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
         float x[8];
         unpack8<T>(rk[p], x);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = __fsub_rn(x[i], km[i]);
+        for (int i = 0; i < 4; ++i) {
+          const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nkm[i]);
+          x[2 * i] = c.x;
+          x[2 * i + 1] = c.y;
+        }
         *reinterpret_cast<uint2*>(k8 + (bh * a.nk + r) * D + vec * 8) = pack_codes(x, sk, rsk);
       }
     }
   }
 
-  // ---- V: per key row (centered when non-causal), codes into the shared tile.
+  // ---- V: per key row (centered when non-causal), fp16 codes into the
+  // shared tile (row-major, rows of kRowWords words).
   {
     float* vscale = reinterpret_cast<float*>(a.ws + L.vscale) + bh * L.nk_pad;
     float* vlog2 = reinterpret_cast<float*>(a.ws + L.vlog2) + bh * L.nk_pad;
@@ -422,9 +470,11 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
       unpack8<T>(rv[p], x);
       float amax = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        x[i] = __fsub_rn(x[i], vm[i]);
-        amax = fmaxf(amax, fabsf(x[i]));
+      for (int i = 0; i < 4; ++i) {
+        const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
+        x[2 * i] = c.x;
+        x[2 * i + 1] = c.y;
+        amax = fmax3(amax, fabsf(c.x), fabsf(c.y));
       }
       if (!valid) amax = 0.0f;
       // The kVpr threads of one row are consecutive lanes.
@@ -432,9 +482,12 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
       for (int o = kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float s = group_scale(amax);
       const float rs = __frcp_rn(s);
-      const uint2 codes = valid ? pack_codes(x, s, rs) : make_uint2(0u, 0u);
-      vrow[lr * kRowWords + 2 * vec] = codes.x;
-      vrow[lr * kRowWords + 2 * vec + 1] = codes.y;
+      const uint4 codes = valid ? pack_codes_f16(x, s, rs) : make_uint4(0u, 0u, 0u, 0u);
+      uint32_t* dst = vrow + lr * kRowWords + 4 * vec;
+      dst[0] = codes.x;
+      dst[1] = codes.y;
+      dst[2] = codes.z;
+      dst[3] = codes.w;
       if (vec == 0) {
         vscale[r] = valid ? s : 0.0f;
         vlog2[r] = valid ? log2f(s) : -INFINITY;
@@ -443,29 +496,65 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
     }
   }
   __syncthreads();
-  // ---- transpose to [D, keys]: each step moves a 4-key x 4-feature block;
-  // the codes are stored as fp16 (the attention kernel's PV operand).
+  // ---- transpose to [D, keys]: each step moves 4 keys x 2 features (one
+  // word of each of 4 rows); a warp covers 8 key quads x 4 feature pairs, so
+  // its shared loads fall on 32 distinct banks (row stride D/2 + 1 words).
   {
     uint2* v16t = reinterpret_cast<uint2*>(a.ws + L.v8t);
-    constexpr int kBlocks = (D / 4) * (kKeyBlock / 4);
+    constexpr int kPairs = D / 2;
+    constexpr int kBlocks = kPairs * (kKeyBlock / 4);
 #pragma unroll
     for (int blk = tid; blk < kBlocks; blk += kPrepassThreads) {
-      const int kq = blk % (kKeyBlock / 4);
-      const int dq = blk / (kKeyBlock / 4);
-      const uint32_t w0 = vrow[(4 * kq + 0) * kRowWords + dq];
-      const uint32_t w1 = vrow[(4 * kq + 1) * kRowWords + dq];
-      const uint32_t w2 = vrow[(4 * kq + 2) * kRowWords + dq];
-      const uint32_t w3 = vrow[(4 * kq + 3) * kRowWords + dq];
-      const uint32_t t0 = __byte_perm(w0, w1, 0x5140), t1 = __byte_perm(w2, w3, 0x5140);
-      const uint32_t t2 = __byte_perm(w0, w1, 0x7362), t3 = __byte_perm(w2, w3, 0x7362);
-      const uint32_t o[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632), __byte_perm(t2, t3, 0x5410),
-                             __byte_perm(t2, t3, 0x7632)};
+      const int kq = (blk % 8) + 8 * (blk / (8 * kPairs));
+      const int dp = (blk / 8) % kPairs;
+      const uint32_t w0 = vrow[(4 * kq + 0) * kRowWords + dp];
+      const uint32_t w1 = vrow[(4 * kq + 1) * kRowWords + dp];
+      const uint32_t w2 = vrow[(4 * kq + 2) * kRowWords + dp];
+      const uint32_t w3 = vrow[(4 * kq + 3) * kRowWords + dp];
       // 8-byte index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and row0 are multiples of 64.
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v16t[((bh * D + 4 * dq + j) * L.nk_pad + row0) / 4 + kq] = codes_to_f16x4(o[j]);
+      const int64_t i0 = ((bh * D + 2 * dp) * L.nk_pad + row0) / 4 + kq;
+      v16t[i0] = make_uint2(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410));
+      v16t[i0 + L.nk_pad / 4] = make_uint2(__byte_perm(w0, w1, 0x7632), __byte_perm(w2, w3, 0x7632));
     }
   }
+}
+
+// One 64-row tile of Q, K and V per CTA, all raw 16-byte loads issued up
+// front.  A persistent form with the next tiles staged in shared memory by
+// bulk copies, two CTAs per SM, was measured 36% slower on c4: the kernel is
+// held by the latency of its arithmetic, which more resident warps hide.
+template <typename T, int D, bool kVec16>
+// Three CTAs per SM (80 registers, a few spilled) beat two at 111 registers
+// by about 10% on the whole prepass: more 16-byte loads in flight.
+__global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArgs a) {
+  constexpr int kVpr = D / 8;
+  constexpr int kRpp = kPrepassThreads / kVpr;
+  constexpr int kPasses = kKeyBlock / kRpp;
+  constexpr int kRowWords = D / 2 + 1;
+  constexpr int kWarps = kPrepassThreads / 32;
+  __shared__ float red[kWarps][3];
+  __shared__ uint32_t vrow[kKeyBlock * kRowWords];
+
+  const int tile = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int64_t b = bh / a.heads, h = bh % a.heads;
+  const int tid = threadIdx.x;
+  const int vec = tid % kVpr;
+  const int ro = tid / kVpr;
+  const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
+  const T* qb = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + vec * 8;
+  const T* kb = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + vec * 8;
+  const T* vb = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + vec * 8;
+  uint4 rq[kPasses], rk[kPasses], rv[kPasses];
+#pragma unroll
+  for (int p = 0; p < kPasses; ++p) {
+    const int64_t r = row0 + ro + p * kRpp;
+    rq[p] = (r < a.nq) ? load_raw8<T, kVec16>(qb + r * a.qs[2]) : make_uint4(0u, 0u, 0u, 0u);
+    const bool kv_ok = r < a.nk;
+    rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + r * a.ks[2]) : make_uint4(0u, 0u, 0u, 0u);
+    rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + r * a.vs[2]) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  quantize_tile<T, D>(a, bh, tile, rq, rk, rv, vrow, red);
 }
 
 }  // namespace piper

@@ -33,6 +33,13 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Largest of three floats (a NaN input is ignored, as by fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ---------------------------------------------------------------- mbarrier
 // Barriers and flags are addressed by 32-bit shared-window addresses
 // (smem_u32), which keeps them out of 64-bit generic registers.

@@ -121,3 +121,18 @@ def test_prepass_rectangular_and_strided_inputs() -> None:
     k2 = torch.randn((1, 1, 64, 64), generator=g).to(torch.float16)
     _check_against_oracle(q2, k2, k2, False)
     assert dev.type == "cuda"
+
+
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_prepass_row_strided_inputs(is_causal: bool) -> None:
+    # [B, N, H, D] storage viewed as [B, H, N, D]: consecutive rows of one
+    # head are H*D elements apart.  1100 rows give three 512-row column-sum
+    # chunks (the last one ragged) and a ragged last 64-row tile.
+    require_b200()
+    g = torch.Generator().manual_seed(6)
+    storage = torch.randn((2, 1100, 3, 128), generator=g).to(torch.bfloat16)
+    q = storage.permute(0, 2, 1, 3)
+    k = (storage * 0.5 + 2.0).permute(0, 2, 1, 3)
+    v = (storage.roll(5, dims=3) - 1.0).permute(0, 2, 1, 3)
+    assert q.stride(2) == 3 * 128
+    _check_against_oracle(q, k, v, is_causal)

@@ -8,8 +8,10 @@ pin the arithmetic tricks they use, exhaustively over the codes:
 * one fused multiply-add with the power-of-two multiples ``512*w`` and
   ``-1024*w`` of the fp16 weight gives ``c*w`` rounded once to fp16, without
   overflow over the weights the kernel can produce (attention.cuh, kPScale);
-* an INT8 V code placed, plus 128, under the fp16 exponent of 1024 and
-  reduced by 1152 is the code itself (prepass.cuh, codes_to_f16x4).
+* an INT8 V code read back from the ``+1.5*2^23`` rounding add converts to
+  fp16 exactly, and the two permutes of the V transpose pick one feature of
+  two keys from two rows' fp16 pairs (prepass.cuh, pack_codes_f16 and
+  quantize_tile).
 """
 
 from __future__ import annotations
@@ -63,12 +65,29 @@ def test_weighting_is_one_rounding_of_code_times_weight() -> None:
 
 
 def test_int8_codes_convert_to_fp16_exactly() -> None:
-    codes = np.arange(-128, 128, dtype=np.int64)
-    for c in codes:
-        u = (int(c) & 0xFF) ^ 0x80  # c + 128 as a byte
-        word = byte_perm(u | (u << 8) | (u << 16) | (u << 24), 0x64646464, 0x5140)
-        h = halves(word).astype(np.float32)
-        assert h[0] - 1152.0 == c and h[1] - 1152.0 == c
+    # round_codes leaves t = 1.5*2^23 + c (c the rounded, clamped code);
+    # pack_codes_f16 subtracts 1.5*2^23 in fp32 and converts the pair to fp16.
+    for c in range(-127, 128):
+        t = np.float32(K_BIAS) + np.float32(c)
+        assert f32_bits(float(t)) & 0xFF == c & 0xFF  # the byte pack_codes stores
+        back = np.float32(t) - np.float32(K_BIAS)
+        assert float(back) == c and float(np.float16(back)) == c
+
+
+def test_v_transpose_permutes_pick_one_feature_of_two_keys() -> None:
+    # The V tile holds, per key row, words of fp16 pairs (feature 2p in the low
+    # half, 2p + 1 in the high half).  0x5410 takes the low halves of rows k
+    # and k + 1, 0x7632 the high halves: feature 2p, then 2p + 1, of both keys.
+    rng = np.random.default_rng(3)
+    for _ in range(200):
+        k0 = rng.integers(-127, 128, size=2).astype(np.float16)
+        k1 = rng.integers(-127, 128, size=2).astype(np.float16)
+        w0 = int(k0.view(np.uint32)[0])
+        w1 = int(k1.view(np.uint32)[0])
+        lo = halves(byte_perm(w0, w1, 0x5410))
+        hi = halves(byte_perm(w0, w1, 0x7632))
+        assert lo[0] == k0[0] and lo[1] == k1[0]
+        assert hi[0] == k0[1] and hi[1] == k1[1]
 
 
 def test_polynomial_exp2_emulated_in_fp32() -> None:
