@@ -329,13 +329,14 @@ __device__ __forceinline__ float absmax_pair_to_f32(uint32_t m) {
 // are transposed 4 keys x 2 features at a time with two permutes and written
 // as [D, keys] with 8-byte stores.  Contains CTA-wide barriers: every thread
 // of the CTA calls it for the same tile.  `vrow` is the padded V code tile,
-// `red` the per-warp maxima.
+// `red` the per-warp maxima, `vstat` (2 x 64 floats) and `gsc` (6 floats) the
+// V row and Q/K group scales with their reciprocals.
 template <typename T, int D>
 __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, int tile,
                                               const uint4 (&rq)[kKeyBlock / (kPrepassThreads / (D / 8))],
                                               const uint4 (&rk)[kKeyBlock / (kPrepassThreads / (D / 8))],
                                               const uint4 (&rv)[kKeyBlock / (kPrepassThreads / (D / 8))],
-                                              uint32_t* vrow, float (*red)[3]) {
+                                              uint32_t* vrow, float (*red)[3], float* vstat, float* gsc) {
   constexpr int kVpr = D / 8;                   // 16-byte vectors per row
   constexpr int kRpp = kPrepassThreads / kVpr;  // rows per pass
   constexpr int kPasses = kKeyBlock / kRpp;     // passes over the 64-row tile
@@ -401,19 +402,55 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
 #pragma unroll
     for (int c = 0; c < 3; ++c) red[warp][c] = am[c];
   }
-  __syncthreads();
+  // Each V row's max (centered when non-causal; zero past the sequence end):
+  // a shuffle among the kVpr consecutive lanes of that row.
+  if (has_kv) {
 #pragma unroll
-  for (int c = 0; c < 3; ++c) {
+    for (int p = 0; p < kPasses; ++p) {
+      const int lr = ro + p * kRpp;
+      float x[8];
+      unpack8<T>(rv[p], x);
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
+        amax = fmax3(amax, fabsf(c.x), fabsf(c.y));
+      }
+      if (row0 + lr >= a.nk) amax = 0.0f;
+#pragma unroll
+      for (int o = kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (vec == 0) vstat[lr] = amax;
+    }
+  }
+  __syncthreads();
+  // Scales, computed once: the Q and K group scales and reciprocals by
+  // threads 0-2, each V row's scale, reciprocal and log2 by thread `row`
+  // (the same IEEE operations on the same maxima as every thread did before).
+  if (tid < 3) {
     float m = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[w][c]);
-    am[c] = m;
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[w][tid]);
+    const float sc = group_scale(m);
+    gsc[tid] = sc;
+    gsc[3 + tid] = __frcp_rn(sc);
   }
+  if (has_kv && tid < kKeyBlock) {
+    const int64_t r = row0 + tid;
+    const bool valid = r < a.nk;
+    const float sv = group_scale(vstat[tid]);
+    const float rsv = __frcp_rn(sv);
+    vstat[tid] = sv;
+    vstat[kKeyBlock + tid] = rsv;
+    reinterpret_cast<float*>(a.ws + L.vscale)[bh * L.nk_pad + r] = valid ? sv : 0.0f;
+    reinterpret_cast<float*>(a.ws + L.vlog2)[bh * L.nk_pad + r] = valid ? log2f(sv) : -INFINITY;
+    reinterpret_cast<float*>(a.ws + L.vrcp)[bh * L.nk_pad + r] = valid ? rsv : 0.0f;
+  }
+  __syncthreads();
 
   // ---- Q codes.
   if (has_q) {
-    const float sq[2] = {group_scale(am[0]), group_scale(am[1])};
-    const float rq2[2] = {__frcp_rn(sq[0]), __frcp_rn(sq[1])};
+    const float sq[2] = {gsc[0], gsc[1]};
+    const float rq2[2] = {gsc[3], gsc[4]};
     int8_t* q8 = reinterpret_cast<int8_t*>(a.ws + L.q8);
     if (tid < 2) {
       const int64_t g = row0 / kQueryGroup + tid;
@@ -434,8 +471,8 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
 
   // ---- K codes (centered by the sequence mean).
   {
-    const float sk = group_scale(am[2]);
-    const float rsk = __frcp_rn(sk);
+    const float sk = gsc[2];
+    const float rsk = gsc[5];
     int8_t* k8 = reinterpret_cast<int8_t*>(a.ws + L.k8);
     if (tid == 0) reinterpret_cast<float*>(a.ws + L.kscale)[bh * L.k_groups + tile] = sk;
 #pragma unroll
@@ -458,41 +495,24 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
   // ---- V: per key row (centered when non-causal), fp16 codes into the
   // shared tile (row-major, rows of kRowWords words).
   {
-    float* vscale = reinterpret_cast<float*>(a.ws + L.vscale) + bh * L.nk_pad;
-    float* vlog2 = reinterpret_cast<float*>(a.ws + L.vlog2) + bh * L.nk_pad;
-    float* vrcp = reinterpret_cast<float*>(a.ws + L.vrcp) + bh * L.nk_pad;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
       const int lr = ro + p * kRpp;
-      const int64_t r = row0 + lr;
-      const bool valid = r < a.nk;
+      const bool valid = row0 + lr < a.nk;
       float x[8];
       unpack8<T>(rv[p], x);
-      float amax = 0.0f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
         x[2 * i] = c.x;
         x[2 * i + 1] = c.y;
-        amax = fmax3(amax, fabsf(c.x), fabsf(c.y));
       }
-      if (!valid) amax = 0.0f;
-      // The kVpr threads of one row are consecutive lanes.
-#pragma unroll
-      for (int o = kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float s = group_scale(amax);
-      const float rs = __frcp_rn(s);
-      const uint4 codes = valid ? pack_codes_f16(x, s, rs) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 codes = valid ? pack_codes_f16(x, vstat[lr], vstat[kKeyBlock + lr]) : make_uint4(0u, 0u, 0u, 0u);
       uint32_t* dst = vrow + lr * kRowWords + 4 * vec;
       dst[0] = codes.x;
       dst[1] = codes.y;
       dst[2] = codes.z;
       dst[3] = codes.w;
-      if (vec == 0) {
-        vscale[r] = valid ? s : 0.0f;
-        vlog2[r] = valid ? log2f(s) : -INFINITY;
-        vrcp[r] = valid ? rs : 0.0f;
-      }
     }
   }
   __syncthreads();
@@ -534,6 +554,8 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
   constexpr int kWarps = kPrepassThreads / 32;
   __shared__ float red[kWarps][3];
   __shared__ uint32_t vrow[kKeyBlock * kRowWords];
+  __shared__ float vstat[2 * kKeyBlock];  // V row maxima, then scales and reciprocals
+  __shared__ float gsc[6];                // Q, Q, K group scales, then their reciprocals
 
   const int tile = blockIdx.x;
   const int64_t bh = blockIdx.y;
@@ -554,7 +576,7 @@ __global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArg
     rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + r * a.ks[2]) : make_uint4(0u, 0u, 0u, 0u);
     rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + r * a.vs[2]) : make_uint4(0u, 0u, 0u, 0u);
   }
-  quantize_tile<T, D>(a, bh, tile, rq, rk, rv, vrow, red);
+  quantize_tile<T, D>(a, bh, tile, rq, rk, rv, vrow, red, vstat, gsc);
 }
 
 }  // namespace piper
