@@ -544,9 +544,10 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
 // bulk copies, two CTAs per SM, was measured 36% slower on c4: the kernel is
 // held by the latency of its arithmetic, which more resident warps hide.
 template <typename T, int D, bool kVec16>
-// Three CTAs per SM (80 registers, a few spilled) beat two at 111 registers
-// by about 10% on the whole prepass: more 16-byte loads in flight.
-__global__ void __launch_bounds__(kPrepassThreads, 3) quantize_kernel(PrepassArgs a) {
+// Resident CTAs per SM, measured: at D = 128 three (80 registers, a few
+// spilled) beat two (114, no spills) by 3% and four (64, 212 bytes spilled) by
+// 7%; at D = 64 four (64 registers) beat three by 6%.
+__global__ void __launch_bounds__(kPrepassThreads, D == 64 ? 4 : 3) quantize_kernel(PrepassArgs a) {
   constexpr int kVpr = D / 8;
   constexpr int kRpp = kPrepassThreads / kVpr;
   constexpr int kPasses = kKeyBlock / kRpp;
