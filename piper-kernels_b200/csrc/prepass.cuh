@@ -350,6 +350,9 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
   const auto& L = a.L;
   const bool has_q = row0 < a.nq;
   const bool has_kv = row0 < a.nk;
+  // Rows of this tile inside each sequence (0..64), for 32-bit row tests.
+  const int nvq = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nq - row0)));
+  const int nvk = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nk - row0)));
   float km[8], vm[8];
   {
     const float* kmean = reinterpret_cast<const float*>(a.ws + L.kmean) + bh * D + vec * 8;
@@ -376,10 +379,9 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
     float kmx = 0.0f;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int64_t r = row0 + ro + p * kRpp;
       const int g = (p * kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
       qm[g] = absmax8<T>(rq[p], qm[g]);
-      if (r < a.nk) {
+      if (ro + p * kRpp < nvk) {
         float x[8];
         unpack8<T>(rk[p], x);
 #pragma unroll
@@ -416,7 +418,7 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
         const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
         amax = fmax3(amax, fabsf(c.x), fabsf(c.y));
       }
-      if (row0 + lr >= a.nk) amax = 0.0f;
+      if (lr >= nvk) amax = 0.0f;
 #pragma unroll
       for (int o = kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       if (vec == 0) vstat[lr] = amax;
@@ -436,7 +438,7 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
   }
   if (has_kv && tid < kKeyBlock) {
     const int64_t r = row0 + tid;
-    const bool valid = r < a.nk;
+    const bool valid = tid < nvk;
     const float sv = group_scale(vstat[tid]);
     const float rsv = __frcp_rn(sv);
     vstat[tid] = sv;
@@ -451,19 +453,19 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
   if (has_q) {
     const float sq[2] = {gsc[0], gsc[1]};
     const float rq2[2] = {gsc[3], gsc[4]};
-    int8_t* q8 = reinterpret_cast<int8_t*>(a.ws + L.q8);
+    // This thread's first code row; later passes are kRpp rows further on.
+    int8_t* q8 = reinterpret_cast<int8_t*>(a.ws + L.q8) + ((bh * a.nq + row0 + ro) * D + vec * 8);
     if (tid < 2) {
       const int64_t g = row0 / kQueryGroup + tid;
       if (g < L.q_groups) reinterpret_cast<float*>(a.ws + L.qscale)[bh * L.q_groups + g] = sq[tid];
     }
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int64_t r = row0 + ro + p * kRpp;
-      if (r < a.nq) {
+      if (ro + p * kRpp < nvq) {
         const int g = (p * kRpp) / kQueryGroup;
         float x[8];
         unpack8<T>(rq[p], x);
-        *reinterpret_cast<uint2*>(q8 + (bh * a.nq + r) * D + vec * 8) = pack_codes(x, sq[g], rq2[g]);
+        *reinterpret_cast<uint2*>(q8 + p * kRpp * D) = pack_codes(x, sq[g], rq2[g]);
       }
     }
   }
@@ -473,12 +475,11 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
   {
     const float sk = gsc[2];
     const float rsk = gsc[5];
-    int8_t* k8 = reinterpret_cast<int8_t*>(a.ws + L.k8);
+    int8_t* k8 = reinterpret_cast<int8_t*>(a.ws + L.k8) + ((bh * a.nk + row0 + ro) * D + vec * 8);
     if (tid == 0) reinterpret_cast<float*>(a.ws + L.kscale)[bh * L.k_groups + tile] = sk;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int64_t r = row0 + ro + p * kRpp;
-      if (r < a.nk) {
+      if (ro + p * kRpp < nvk) {
         float x[8];
         unpack8<T>(rk[p], x);
 #pragma unroll
@@ -487,7 +488,7 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
           x[2 * i] = c.x;
           x[2 * i + 1] = c.y;
         }
-        *reinterpret_cast<uint2*>(k8 + (bh * a.nk + r) * D + vec * 8) = pack_codes(x, sk, rsk);
+        *reinterpret_cast<uint2*>(k8 + p * kRpp * D) = pack_codes(x, sk, rsk);
       }
     }
   }
@@ -498,7 +499,7 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
       const int lr = ro + p * kRpp;
-      const bool valid = row0 + lr < a.nk;
+      const bool valid = lr < nvk;
       float x[8];
       unpack8<T>(rv[p], x);
 #pragma unroll
@@ -520,7 +521,10 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
   // word of each of 4 rows); a warp covers 8 key quads x 4 feature pairs, so
   // its shared loads fall on 32 distinct banks (row stride D/2 + 1 words).
   {
-    uint2* v16t = reinterpret_cast<uint2*>(a.ws + L.v8t);
+    // 8-byte index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and
+    // row0 are multiples of 64.
+    uint2* v16t = reinterpret_cast<uint2*>(a.ws + L.v8t) + (bh * D * L.nk_pad + row0) / 4;
+    const int64_t row_words = L.nk_pad / 4;  // one feature row, in 8-byte units
     constexpr int kPairs = D / 2;
     constexpr int kBlocks = kPairs * (kKeyBlock / 4);
 #pragma unroll
@@ -531,10 +535,9 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
       const uint32_t w1 = vrow[(4 * kq + 1) * kRowWords + dp];
       const uint32_t w2 = vrow[(4 * kq + 2) * kRowWords + dp];
       const uint32_t w3 = vrow[(4 * kq + 3) * kRowWords + dp];
-      // 8-byte index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and row0 are multiples of 64.
-      const int64_t i0 = ((bh * D + 2 * dp) * L.nk_pad + row0) / 4 + kq;
-      v16t[i0] = make_uint2(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410));
-      v16t[i0 + L.nk_pad / 4] = make_uint2(__byte_perm(w0, w1, 0x7632), __byte_perm(w2, w3, 0x7632));
+      uint2* out = v16t + (2 * dp) * row_words + kq;
+      out[0] = make_uint2(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410));
+      out[row_words] = make_uint2(__byte_perm(w0, w1, 0x7632), __byte_perm(w2, w3, 0x7632));
     }
   }
 }
