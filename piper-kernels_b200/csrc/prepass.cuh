@@ -137,14 +137,20 @@ __global__ void __launch_bounds__(kPrepassThreads, 2) kv_sum_kernel(PrepassArgs 
   // keeps kUnroll (K only) or 2 kUnroll (K and V) 16-byte loads in flight.
   constexpr int kUnroll = 8;
   int64_t r = r0 + ro;
+  // Row pointers advanced by precomputed steps (no 64-bit multiply per load).
+  const int64_t kstep = kRpp * a.ks[2], vstep = kRpp * a.vs[2];
+  const T* kp = kbase + r * a.ks[2];
+  const T* vp = vbase + r * a.vs[2];
   for (; r + (kUnroll - 1) * kRpp < r1; r += kUnroll * kRpp) {
     uint4 rk[kUnroll], rv[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) rk[u] = load_raw8<T, kVec16>(kbase + (r + u * kRpp) * a.ks[2]);
+    for (int u = 0; u < kUnroll; ++u) rk[u] = load_raw8<T, kVec16>(kp + u * kstep);
     if (with_v) {
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) rv[u] = load_raw8<T, kVec16>(vbase + (r + u * kRpp) * a.vs[2]);
+      for (int u = 0; u < kUnroll; ++u) rv[u] = load_raw8<T, kVec16>(vp + u * vstep);
     }
+    kp += kUnroll * kstep;
+    vp += kUnroll * vstep;
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       float x[8];
@@ -568,17 +574,22 @@ __global__ void __launch_bounds__(kPrepassThreads, D == 64 ? 4 : 3) quantize_ker
   const int vec = tid % kVpr;
   const int ro = tid / kVpr;
   const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
-  const T* qb = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + vec * 8;
-  const T* kb = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + vec * 8;
-  const T* vb = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + vec * 8;
+  // This thread's first row of each tensor; pass p is p * kRpp rows further.
+  const int64_t r = row0 + ro;
+  const T* qb = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + r * a.qs[2] + vec * 8;
+  const T* kb = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + r * a.ks[2] + vec * 8;
+  const T* vb = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + r * a.vs[2] + vec * 8;
+  const int64_t qstep = kRpp * a.qs[2], kstep = kRpp * a.ks[2], vstep = kRpp * a.vs[2];
+  const int nvq = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nq - row0)));
+  const int nvk = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nk - row0)));
   uint4 rq[kPasses], rk[kPasses], rv[kPasses];
 #pragma unroll
   for (int p = 0; p < kPasses; ++p) {
-    const int64_t r = row0 + ro + p * kRpp;
-    rq[p] = (r < a.nq) ? load_raw8<T, kVec16>(qb + r * a.qs[2]) : make_uint4(0u, 0u, 0u, 0u);
-    const bool kv_ok = r < a.nk;
-    rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + r * a.ks[2]) : make_uint4(0u, 0u, 0u, 0u);
-    rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + r * a.vs[2]) : make_uint4(0u, 0u, 0u, 0u);
+    const int lr = ro + p * kRpp;
+    rq[p] = (lr < nvq) ? load_raw8<T, kVec16>(qb + p * qstep) : make_uint4(0u, 0u, 0u, 0u);
+    const bool kv_ok = lr < nvk;
+    rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + p * kstep) : make_uint4(0u, 0u, 0u, 0u);
+    rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + p * vstep) : make_uint4(0u, 0u, 0u, 0u);
   }
   quantize_tile<T, D>(a, bh, tile, rq, rk, rv, vrow, red, vstat, gsc);
 }
