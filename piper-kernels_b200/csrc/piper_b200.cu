@@ -203,7 +203,8 @@ enum PrepassPart { kSums = 1, kFinalize = 2, kQuantize = 4 };
 template <typename T, int D, bool V16>
 void launch_prepass_t(const piper::PrepassArgs& a, int64_t bh, int parts, cudaStream_t stream) {
   if (parts & kSums) {
-    const dim3 sum_grid(static_cast<unsigned>(a.L.chunks), static_cast<unsigned>(bh));
+    // One CTA per (chunk, head, tensor): K, and V unless causal.
+    const dim3 sum_grid(static_cast<unsigned>(a.L.chunks), static_cast<unsigned>(bh), a.causal ? 1u : 2u);
     piper::kv_sum_kernel<T, D, V16><<<sum_grid, piper::kPrepassThreads, 0, stream>>>(a);
   }
   if (parts & kFinalize) piper::finalize_means_kernel<D><<<static_cast<unsigned>(bh), D, 0, stream>>>(a);
