@@ -210,7 +210,9 @@ void launch_prepass_t(const piper::PrepassArgs& a, int64_t bh, int parts, cudaSt
   if (parts & kFinalize) piper::finalize_means_kernel<D><<<static_cast<unsigned>(bh), D, 0, stream>>>(a);
   if (parts & kQuantize) {
     const int64_t tiles = (std::max(a.nq, a.nk) + piper::kKeyBlock - 1) / piper::kKeyBlock;
-    const dim3 q_grid(static_cast<unsigned>(tiles), static_cast<unsigned>(bh));
+    // At D = 128 one CTA per (tile, head, tensor): Q, K, V; at D = 64 one per
+    // (tile, head).
+    const dim3 q_grid(static_cast<unsigned>(tiles), static_cast<unsigned>(bh), D == 128 ? 3u : 1u);
     piper::quantize_kernel<T, D, V16><<<q_grid, piper::kPrepassThreads, 0, stream>>>(a);
   }
 }

@@ -305,123 +305,188 @@ __device__ __forceinline__ float absmax_pair_to_f32(uint32_t m) {
   return fmaxf(to_f32<T>(e[0]), to_f32<T>(e[1]));
 }
 
-// The arithmetic of one 64-row tile of Q, K and V, given each thread's raw
-// 16-byte vectors (rows past a sequence end hold zeros).  The two 32-row Q
-// group maxima (packed 16-bit maxima of the raw values) and the 64-row K
-// group max share one block-wide reduction; each V row's max is a shuffle
-// among the threads of that row.  V codes go row-major as fp16 into a padded
-// shared tile (row stride D/2 + 1 words, so rows fall on distinct banks), then
-// are transposed 4 keys x 2 features at a time with two permutes and written
-// as [D, keys] with 8-byte stores.  Contains CTA-wide barriers: every thread
-// of the CTA calls it for the same tile.  `vrow` is the padded V code tile,
-// `red` the per-warp maxima, `vstat` (2 x 64 floats) and `gsc` (6 floats) the
-// V row and Q/K group scales with their reciprocals.
-template <typename T, int D>
-__device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, int tile,
-                                              const uint4 (&rq)[kKeyBlock / (kPrepassThreads / (D / 8))],
-                                              const uint4 (&rk)[kKeyBlock / (kPrepassThreads / (D / 8))],
-                                              const uint4 (&rv)[kKeyBlock / (kPrepassThreads / (D / 8))],
-                                              uint32_t* vrow, float (*red)[3], float* vstat, float* gsc) {
-  constexpr int kVpr = D / 8;                   // 16-byte vectors per row
-  constexpr int kRpp = kPrepassThreads / kVpr;  // rows per pass
-  constexpr int kPasses = kKeyBlock / kRpp;     // passes over the 64-row tile
-  constexpr int kRowWords = D / 2 + 1;          // padded fp16 V code row, in words
-  constexpr int kWarps = kPrepassThreads / 32;
-  const int tid = threadIdx.x;
-  const int lane = tid % 32, warp = tid / 32;
-  const int vec = tid % kVpr;
-  const int ro = tid / kVpr;
-  const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
-  const auto& L = a.L;
-  const bool has_q = row0 < a.nq;
-  const bool has_kv = row0 < a.nk;
-  // Rows of this tile inside each sequence (0..64), for 32-bit row tests.
-  const int nvq = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nq - row0)));
-  const int nvk = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nk - row0)));
-  float km[8], vm[8];
-  {
-    const float* kmean = reinterpret_cast<const float*>(a.ws + L.kmean) + bh * D + vec * 8;
-    const float* vmean = reinterpret_cast<const float*>(a.ws + L.vmean) + bh * D + vec * 8;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      km[i] = has_kv ? kmean[i] : 0.0f;
-      vm[i] = (has_kv && !a.causal) ? vmean[i] : 0.0f;
-    }
-  }
-  // Negated means in pairs: x - m is computed as x + (-m), the same IEEE result.
-  float2 nkm[4], nvm[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    nkm[i] = make_float2(-km[2 * i], -km[2 * i + 1]);
-    nvm[i] = make_float2(-vm[2 * i], -vm[2 * i + 1]);
-  }
+// One 64-row tile of one tensor per CTA.  Each thread holds its raw 16-byte
+// vectors of that tensor (rows past the sequence end hold zeros).  The
+// functions below contain CTA-wide barriers, and every thread of the CTA calls
+// one of them for the same tile.
+template <int D>
+struct QuantTile {
+  static constexpr int kVpr = D / 8;                   // 16-byte vectors per row
+  static constexpr int kRpp = kPrepassThreads / kVpr;  // rows per pass
+  static constexpr int kPasses = kKeyBlock / kRpp;     // passes over the 64-row tile
+  static constexpr int kRowWords = D / 2 + 1;          // padded fp16 V code row, in words
+  static constexpr int kWarps = kPrepassThreads / 32;
+};
 
-  // ---- group maxima: Q (two 32-row groups) and centered K (one 64-row group);
-  // rows past the sequence end count as zero, as the reference's zero padding.
-  float am[3];
-  {
-    uint32_t qm[2] = {0u, 0u};  // packed |q| maxima of the two Q groups
-    float kmx = 0.0f;
+// Largest value of `v` over the CTA, through the per-warp slots red[][c]
+// (two barriers; the result is the same in every thread).
+template <int D>
+__device__ __forceinline__ float cta_max(float v, float (*red)[2], int c) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
 #pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      const int g = (p * kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
-      qm[g] = absmax8<T>(rq[p], qm[g]);
-      if (ro + p * kRpp < nvk) {
-        float x[8];
-        unpack8<T>(rk[p], x);
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) red[warp][c] = v;
+  __syncthreads();
+  float m = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nkm[i]);
-          kmx = fmax3(kmx, fabsf(c.x), fabsf(c.y));
-        }
-      }
-    }
-    am[0] = absmax_pair_to_f32<T>(qm[0]);
-    am[1] = absmax_pair_to_f32<T>(qm[1]);
-    am[2] = kmx;
+  for (int w = 0; w < QuantTile<D>::kWarps; ++w) m = fmaxf(m, red[w][c]);
+  return m;
+}
+
+// Q codes of one tile: two 32-row groups, each scale from the packed 16-bit
+// maxima of the raw values (exact in the input type, so equal to the fp32
+// maximum; rows past the sequence end count as zero, as the reference's zero
+// padding).
+template <typename T, int D>
+__device__ __forceinline__ void quantize_q_tile(const PrepassArgs& a, int64_t bh, int tile,
+                                                const uint4 (&rq)[QuantTile<D>::kPasses], float (*red)[2],
+                                                float* gsc) {
+  using Q = QuantTile<D>;
+  const int tid = threadIdx.x;
+  const int vec = tid % Q::kVpr, ro = tid / Q::kVpr;
+  const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
+  const int nvq = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nq - row0)));
+  uint32_t qm[2] = {0u, 0u};
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p) {
+    const int g = (p * Q::kRpp) / kQueryGroup;  // compile-time: kRpp divides or is divided by 32
+    qm[g] = absmax8<T>(rq[p], qm[g]);
   }
+  float m0 = absmax_pair_to_f32<T>(qm[0]), m1 = absmax_pair_to_f32<T>(qm[1]);
+  const int lane = tid % 32, warp = tid / 32;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-    for (int c = 0; c < 3; ++c) am[c] = fmaxf(am[c], __shfl_xor_sync(0xffffffffu, am[c], o));
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
   }
   if (lane == 0) {
-#pragma unroll
-    for (int c = 0; c < 3; ++c) red[warp][c] = am[c];
-  }
-  // Each V row's max (centered when non-causal; zero past the sequence end):
-  // a shuffle among the kVpr consecutive lanes of that row.
-  if (has_kv) {
-#pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      const int lr = ro + p * kRpp;
-      float x[8];
-      unpack8<T>(rv[p], x);
-      float amax = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
-        amax = fmax3(amax, fabsf(c.x), fabsf(c.y));
-      }
-      if (lr >= nvk) amax = 0.0f;
-#pragma unroll
-      for (int o = kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (vec == 0) vstat[lr] = amax;
-    }
+    red[warp][0] = m0;
+    red[warp][1] = m1;
   }
   __syncthreads();
-  // Scales, computed once: the Q and K group scales and reciprocals by
-  // threads 0-2, each V row's scale, reciprocal and log2 by thread `row`
-  // (the same IEEE operations on the same maxima as every thread did before).
-  if (tid < 3) {
+  // The group scales, computed once (threads 0 and 1).
+  if (tid < 2) {
     float m = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[w][tid]);
+    for (int w = 0; w < Q::kWarps; ++w) m = fmaxf(m, red[w][tid]);
     const float sc = group_scale(m);
     gsc[tid] = sc;
-    gsc[3 + tid] = __frcp_rn(sc);
+    gsc[2 + tid] = __frcp_rn(sc);
+    const int64_t g = row0 / kQueryGroup + tid;
+    if (g < a.L.q_groups) reinterpret_cast<float*>(a.ws + a.L.qscale)[bh * a.L.q_groups + g] = sc;
   }
-  if (has_kv && tid < kKeyBlock) {
+  __syncthreads();
+  // This thread's first code row; later passes are kRpp rows further on.
+  int8_t* q8 = reinterpret_cast<int8_t*>(a.ws + a.L.q8) + ((bh * a.nq + row0 + ro) * D + vec * 8);
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p) {
+    if (ro + p * Q::kRpp < nvq) {
+      const int g = (p * Q::kRpp) / kQueryGroup;
+      float x[8];
+      unpack8<T>(rq[p], x);
+      *reinterpret_cast<uint2*>(q8 + p * Q::kRpp * D) = pack_codes(x, gsc[g], gsc[2 + g]);
+    }
+  }
+}
+
+// K codes of one tile, centered by the sequence mean: one 64-row group.
+template <typename T, int D>
+__device__ __forceinline__ void quantize_k_tile(const PrepassArgs& a, int64_t bh, int tile,
+                                                const uint4 (&rk)[QuantTile<D>::kPasses], float (*red)[2],
+                                                float* gsc) {
+  using Q = QuantTile<D>;
+  const int tid = threadIdx.x;
+  const int vec = tid % Q::kVpr, ro = tid / Q::kVpr;
+  const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
+  const int nvk = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nk - row0)));
+  // Negated means in pairs: x - m is computed as x + (-m), the same IEEE result.
+  float2 nkm[4];
+  {
+    const float* kmean = reinterpret_cast<const float*>(a.ws + a.L.kmean) + bh * D + vec * 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) nkm[i] = make_float2(-kmean[2 * i], -kmean[2 * i + 1]);
+  }
+  float kmx = 0.0f;
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p) {
+    if (ro + p * Q::kRpp < nvk) {
+      float x[8];
+      unpack8<T>(rk[p], x);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nkm[i]);
+        kmx = fmax3(kmx, fabsf(c.x), fabsf(c.y));
+      }
+    }
+  }
+  const float m = cta_max<D>(kmx, red, 0);
+  if (tid == 0) {
+    const float sc = group_scale(m);
+    gsc[0] = sc;
+    gsc[1] = __frcp_rn(sc);
+    reinterpret_cast<float*>(a.ws + a.L.kscale)[bh * a.L.k_groups + tile] = sc;
+  }
+  __syncthreads();
+  const float sk = gsc[0], rsk = gsc[1];
+  int8_t* k8 = reinterpret_cast<int8_t*>(a.ws + a.L.k8) + ((bh * a.nk + row0 + ro) * D + vec * 8);
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p) {
+    if (ro + p * Q::kRpp < nvk) {
+      float x[8];
+      unpack8<T>(rk[p], x);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nkm[i]);
+        x[2 * i] = c.x;
+        x[2 * i + 1] = c.y;
+      }
+      *reinterpret_cast<uint2*>(k8 + p * Q::kRpp * D) = pack_codes(x, sk, rsk);
+    }
+  }
+}
+
+// V codes of one tile: one scale per key row (centered by the sequence mean
+// when non-causal).  Each row's max is a shuffle among the threads of that
+// row; its scale, reciprocal and log2 are computed once, by thread `row`.  V
+// codes go row-major as fp16 into a padded shared tile (row stride D/2 + 1
+// words, so rows fall on distinct banks), then are transposed 4 keys x 2
+// features at a time with two permutes and written as [D, keys] with 8-byte
+// stores.
+template <typename T, int D>
+__device__ __forceinline__ void quantize_v_tile(const PrepassArgs& a, int64_t bh, int tile,
+                                                const uint4 (&rv)[QuantTile<D>::kPasses], uint32_t* vrow,
+                                                float* vstat) {
+  using Q = QuantTile<D>;
+  const int tid = threadIdx.x;
+  const int vec = tid % Q::kVpr, ro = tid / Q::kVpr;
+  const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
+  const auto& L = a.L;
+  const int nvk = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nk - row0)));
+  float2 nvm[4];
+  {
+    const float* vmean = reinterpret_cast<const float*>(a.ws + L.vmean) + bh * D + vec * 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      nvm[i] = a.causal ? make_float2(-0.0f, -0.0f) : make_float2(-vmean[2 * i], -vmean[2 * i + 1]);
+  }
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p) {
+    const int lr = ro + p * Q::kRpp;
+    float x[8];
+    unpack8<T>(rv[p], x);
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
+      amax = fmax3(amax, fabsf(c.x), fabsf(c.y));
+    }
+    if (lr >= nvk) amax = 0.0f;
+#pragma unroll
+    for (int o = Q::kVpr / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (vec == 0) vstat[lr] = amax;
+  }
+  __syncthreads();
+  if (tid < kKeyBlock) {
     const int64_t r = row0 + tid;
     const bool valid = tid < nvk;
     const float sv = group_scale(vstat[tid]);
@@ -433,144 +498,114 @@ __device__ __forceinline__ void quantize_tile(const PrepassArgs& a, int64_t bh, 
     reinterpret_cast<float*>(a.ws + L.vrcp)[bh * L.nk_pad + r] = valid ? rsv : 0.0f;
   }
   __syncthreads();
-
-  // ---- Q codes.
-  if (has_q) {
-    const float sq[2] = {gsc[0], gsc[1]};
-    const float rq2[2] = {gsc[3], gsc[4]};
-    // This thread's first code row; later passes are kRpp rows further on.
-    int8_t* q8 = reinterpret_cast<int8_t*>(a.ws + L.q8) + ((bh * a.nq + row0 + ro) * D + vec * 8);
-    if (tid < 2) {
-      const int64_t g = row0 / kQueryGroup + tid;
-      if (g < L.q_groups) reinterpret_cast<float*>(a.ws + L.qscale)[bh * L.q_groups + g] = sq[tid];
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p) {
+    const int lr = ro + p * Q::kRpp;
+    float x[8];
+    unpack8<T>(rv[p], x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
+      x[2 * i] = c.x;
+      x[2 * i + 1] = c.y;
     }
-#pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      if (ro + p * kRpp < nvq) {
-        const int g = (p * kRpp) / kQueryGroup;
-        float x[8];
-        unpack8<T>(rq[p], x);
-        *reinterpret_cast<uint2*>(q8 + p * kRpp * D) = pack_codes(x, sq[g], rq2[g]);
-      }
-    }
-  }
-  if (!has_kv) return;
-
-  // ---- K codes (centered by the sequence mean).
-  {
-    const float sk = gsc[2];
-    const float rsk = gsc[5];
-    int8_t* k8 = reinterpret_cast<int8_t*>(a.ws + L.k8) + ((bh * a.nk + row0 + ro) * D + vec * 8);
-    if (tid == 0) reinterpret_cast<float*>(a.ws + L.kscale)[bh * L.k_groups + tile] = sk;
-#pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      if (ro + p * kRpp < nvk) {
-        float x[8];
-        unpack8<T>(rk[p], x);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nkm[i]);
-          x[2 * i] = c.x;
-          x[2 * i + 1] = c.y;
-        }
-        *reinterpret_cast<uint2*>(k8 + p * kRpp * D) = pack_codes(x, sk, rsk);
-      }
-    }
-  }
-
-  // ---- V: per key row (centered when non-causal), fp16 codes into the
-  // shared tile (row-major, rows of kRowWords words).
-  {
-#pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-      const int lr = ro + p * kRpp;
-      const bool valid = lr < nvk;
-      float x[8];
-      unpack8<T>(rv[p], x);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 c = __fadd2_rn(make_float2(x[2 * i], x[2 * i + 1]), nvm[i]);
-        x[2 * i] = c.x;
-        x[2 * i + 1] = c.y;
-      }
-      const uint4 codes = valid ? pack_codes_f16(x, vstat[lr], vstat[kKeyBlock + lr]) : make_uint4(0u, 0u, 0u, 0u);
-      uint32_t* dst = vrow + lr * kRowWords + 4 * vec;
-      dst[0] = codes.x;
-      dst[1] = codes.y;
-      dst[2] = codes.z;
-      dst[3] = codes.w;
-    }
+    const uint4 codes = lr < nvk ? pack_codes_f16(x, vstat[lr], vstat[kKeyBlock + lr]) : make_uint4(0u, 0u, 0u, 0u);
+    uint32_t* dst = vrow + lr * Q::kRowWords + 4 * vec;
+    dst[0] = codes.x;
+    dst[1] = codes.y;
+    dst[2] = codes.z;
+    dst[3] = codes.w;
   }
   __syncthreads();
-  // ---- transpose to [D, keys]: each step moves 4 keys x 2 features (one
-  // word of each of 4 rows); a warp covers 8 key quads x 4 feature pairs, so
-  // its shared loads fall on 32 distinct banks (row stride D/2 + 1 words).
-  {
-    // 8-byte index of (d, key) = ((bh*D + d) * nk_pad + key) / 4; nk_pad and
-    // row0 are multiples of 64.
-    uint2* v16t = reinterpret_cast<uint2*>(a.ws + L.v8t) + (bh * D * L.nk_pad + row0) / 4;
-    const int64_t row_words = L.nk_pad / 4;  // one feature row, in 8-byte units
-    constexpr int kPairs = D / 2;
-    constexpr int kBlocks = kPairs * (kKeyBlock / 4);
+  // Transpose to [D, keys]: each step moves 4 keys x 2 features (one word of
+  // each of 4 rows); a warp covers 8 key quads x 4 feature pairs, so its
+  // shared loads fall on 32 distinct banks.  8-byte index of (d, key) =
+  // ((bh*D + d) * nk_pad + key) / 4; nk_pad and row0 are multiples of 64.
+  uint2* v16t = reinterpret_cast<uint2*>(a.ws + L.v8t) + (bh * D * L.nk_pad + row0) / 4;
+  const int64_t row_words = L.nk_pad / 4;  // one feature row, in 8-byte units
+  constexpr int kPairs = D / 2;
+  constexpr int kBlocks = kPairs * (kKeyBlock / 4);
 #pragma unroll
-    for (int blk = tid; blk < kBlocks; blk += kPrepassThreads) {
-      const int kq = (blk % 8) + 8 * (blk / (8 * kPairs));
-      const int dp = (blk / 8) % kPairs;
-      const uint32_t w0 = vrow[(4 * kq + 0) * kRowWords + dp];
-      const uint32_t w1 = vrow[(4 * kq + 1) * kRowWords + dp];
-      const uint32_t w2 = vrow[(4 * kq + 2) * kRowWords + dp];
-      const uint32_t w3 = vrow[(4 * kq + 3) * kRowWords + dp];
-      uint2* out = v16t + (2 * dp) * row_words + kq;
-      out[0] = make_uint2(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410));
-      out[row_words] = make_uint2(__byte_perm(w0, w1, 0x7632), __byte_perm(w2, w3, 0x7632));
-    }
+  for (int blk = tid; blk < kBlocks; blk += kPrepassThreads) {
+    const int kq = (blk % 8) + 8 * (blk / (8 * kPairs));
+    const int dp = (blk / 8) % kPairs;
+    const uint32_t w0 = vrow[(4 * kq + 0) * Q::kRowWords + dp];
+    const uint32_t w1 = vrow[(4 * kq + 1) * Q::kRowWords + dp];
+    const uint32_t w2 = vrow[(4 * kq + 2) * Q::kRowWords + dp];
+    const uint32_t w3 = vrow[(4 * kq + 3) * Q::kRowWords + dp];
+    uint2* out = v16t + (2 * dp) * row_words + kq;
+    out[0] = make_uint2(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410));
+    out[row_words] = make_uint2(__byte_perm(w0, w1, 0x7632), __byte_perm(w2, w3, 0x7632));
   }
 }
 
-// One 64-row tile of Q, K and V per CTA, all raw 16-byte loads issued up
-// front.  A persistent form with the next tiles staged in shared memory by
+// This thread's raw 16-byte vectors of one tensor's 64-row tile (zeros past
+// the sequence end): all loads issued up front.
+template <typename T, int D, bool kVec16>
+__device__ __forceinline__ void load_tile(const void* src, const int64_t (&st)[3], int64_t b, int64_t h, int64_t row0,
+                                          int64_t rows, uint4 (&raw)[QuantTile<D>::kPasses]) {
+  using Q = QuantTile<D>;
+  const int vec = threadIdx.x % Q::kVpr, ro = threadIdx.x / Q::kVpr;
+  // This thread's first row; pass p is p * kRpp rows further.
+  const T* base = static_cast<const T*>(src) + b * st[0] + h * st[1] + (row0 + ro) * st[2] + vec * 8;
+  const int64_t step = Q::kRpp * st[2];
+  const int nv = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), rows - row0)));
+#pragma unroll
+  for (int p = 0; p < Q::kPasses; ++p)
+    raw[p] = (ro + p * Q::kRpp < nv) ? load_raw8<T, kVec16>(base + p * step) : make_uint4(0u, 0u, 0u, 0u);
+}
+
+// At D = 128, grid (ceil(max(Nq,Nk)/64), B*H, 3): one 64-row tile of one
+// tensor per CTA (blockIdx.z: 0 = Q, 1 = K, 2 = V), four CTAs per SM (62
+// registers).  Measured against one CTA quantizing all three tensors of a tile
+// (three CTAs per SM, 80 registers), over two runs: 3-6% faster on c4, 4-6% on
+// c2, 6-9% on causal c3.  At D = 64, grid (..., B*H, 1): one CTA loads all
+// three tensors' tile and quantizes Q, K, V in turn, four CTAs per SM; the
+// split form is 9-15% slower there (half-size tiles: the per-CTA barriers and
+// scale work weigh more), and this form is 3% slower than the former
+// single-function kernel (more barriers).  A persistent form with the next tiles staged in shared memory by
 // bulk copies, two CTAs per SM, was measured 36% slower on c4: the kernel is
 // held by the latency of its arithmetic, which more resident warps hide.
 template <typename T, int D, bool kVec16>
-// Resident CTAs per SM, measured: at D = 128 three (80 registers, a few
-// spilled) beat two (114, no spills) by 3% and four (64, 212 bytes spilled) by
-// 7%; at D = 64 four (64 registers) beat three by 6%.
-__global__ void __launch_bounds__(kPrepassThreads, D == 64 ? 4 : 3) quantize_kernel(PrepassArgs a) {
-  constexpr int kVpr = D / 8;
-  constexpr int kRpp = kPrepassThreads / kVpr;
-  constexpr int kPasses = kKeyBlock / kRpp;
-  constexpr int kRowWords = D / 2 + 1;
-  constexpr int kWarps = kPrepassThreads / 32;
-  __shared__ float red[kWarps][3];
-  __shared__ uint32_t vrow[kKeyBlock * kRowWords];
+__global__ void __launch_bounds__(kPrepassThreads, 4) quantize_kernel(PrepassArgs a) {
+  using Q = QuantTile<D>;
+  __shared__ float red[Q::kWarps][2];
+  __shared__ uint32_t vrow[kKeyBlock * Q::kRowWords];
   __shared__ float vstat[2 * kKeyBlock];  // V row maxima, then scales and reciprocals
-  __shared__ float gsc[6];                // Q, Q, K group scales, then their reciprocals
+  __shared__ float gsc[4];                // group scales and their reciprocals
 
   const int tile = blockIdx.x;
   const int64_t bh = blockIdx.y;
   const int64_t b = bh / a.heads, h = bh % a.heads;
-  const int tid = threadIdx.x;
-  const int vec = tid % kVpr;
-  const int ro = tid / kVpr;
   const int64_t row0 = static_cast<int64_t>(tile) * kKeyBlock;
-  // This thread's first row of each tensor; pass p is p * kRpp rows further.
-  const int64_t r = row0 + ro;
-  const T* qb = static_cast<const T*>(a.q) + b * a.qs[0] + h * a.qs[1] + r * a.qs[2] + vec * 8;
-  const T* kb = static_cast<const T*>(a.k) + b * a.ks[0] + h * a.ks[1] + r * a.ks[2] + vec * 8;
-  const T* vb = static_cast<const T*>(a.v) + b * a.vs[0] + h * a.vs[1] + r * a.vs[2] + vec * 8;
-  const int64_t qstep = kRpp * a.qs[2], kstep = kRpp * a.ks[2], vstep = kRpp * a.vs[2];
-  const int nvq = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nq - row0)));
-  const int nvk = static_cast<int>(min(int64_t(kKeyBlock), max(int64_t(0), a.nk - row0)));
-  uint4 rq[kPasses], rk[kPasses], rv[kPasses];
-#pragma unroll
-  for (int p = 0; p < kPasses; ++p) {
-    const int lr = ro + p * kRpp;
-    rq[p] = (lr < nvq) ? load_raw8<T, kVec16>(qb + p * qstep) : make_uint4(0u, 0u, 0u, 0u);
-    const bool kv_ok = lr < nvk;
-    rk[p] = kv_ok ? load_raw8<T, kVec16>(kb + p * kstep) : make_uint4(0u, 0u, 0u, 0u);
-    rv[p] = kv_ok ? load_raw8<T, kVec16>(vb + p * vstep) : make_uint4(0u, 0u, 0u, 0u);
+  if constexpr (D == 128) {
+    const int part = blockIdx.z;
+    const int64_t rows = part == 0 ? a.nq : a.nk;
+    if (row0 >= rows) return;  // the whole CTA: this tensor has no rows here
+    uint4 raw[Q::kPasses];
+    if (part == 0) {
+      load_tile<T, D, kVec16>(a.q, a.qs, b, h, row0, a.nq, raw);
+      quantize_q_tile<T, D>(a, bh, tile, raw, red, gsc);
+    } else if (part == 1) {
+      load_tile<T, D, kVec16>(a.k, a.ks, b, h, row0, a.nk, raw);
+      quantize_k_tile<T, D>(a, bh, tile, raw, red, gsc);
+    } else {
+      load_tile<T, D, kVec16>(a.v, a.vs, b, h, row0, a.nk, raw);
+      quantize_v_tile<T, D>(a, bh, tile, raw, vrow, vstat);
+    }
+  } else {
+    // Q, K and V in turn.  Between the calls, every thread passes a barrier
+    // of the next call before any thread writes `red` or `gsc` again.
+    uint4 rq[Q::kPasses], rk[Q::kPasses], rv[Q::kPasses];
+    load_tile<T, D, kVec16>(a.q, a.qs, b, h, row0, a.nq, rq);
+    load_tile<T, D, kVec16>(a.k, a.ks, b, h, row0, a.nk, rk);
+    load_tile<T, D, kVec16>(a.v, a.vs, b, h, row0, a.nk, rv);
+    if (row0 < a.nq) quantize_q_tile<T, D>(a, bh, tile, rq, red, gsc);
+    if (row0 < a.nk) {
+      quantize_k_tile<T, D>(a, bh, tile, rk, red, gsc);
+      quantize_v_tile<T, D>(a, bh, tile, rv, vrow, vstat);
+    }
   }
-  quantize_tile<T, D>(a, bh, tile, rq, rk, rv, vrow, red, vstat, gsc);
 }
 
 }  // namespace piper
