@@ -12,18 +12,22 @@
 // then add), code = clamp(round_half_even(x/scale), -127, 127).
 //
 // Two launches:
-//   kv_sum_kernel      grid (chunks, B*H): 16-byte vector loads of K (and V),
-//                      exact fp64 column sums per 512-row chunk; the last
-//                      chunk of each (b,h) to finish turns the partial sums
+//   kv_sum_kernel      grid (chunks, B*H, 2 or 1): one 512-row chunk of K
+//                      (or of V, when non-causal) per CTA, 16-byte vector
+//                      loads, exact fp64 column sums; the last of a (b,h)'s
+//                      CTAs to finish turns the partial sums of both tensors
 //                      into fp32 means (fixed order, so results are
-//                      deterministic).  For a sequence shard it writes
-//                      the shard's fp64 column totals instead; the caller
-//                      sums them over the ranks and finalize_means_kernel
-//                      divides by the total key count.
-//   quantize_kernel    grid (ceil(max(Nq,Nk)/64), B*H): one 64-row tile of Q,
-//                      K and V per CTA; group amax via warp shuffles + shared
-//                      memory; V codes transposed to [D, keys] through shared
-//                      memory so the attention kernel's PV operand is K-major.
+//                      deterministic).  For a sequence shard it writes the
+//                      shard's fp64 column totals instead; the caller sums
+//                      them over the ranks and finalize_means_kernel divides
+//                      by the total key count.
+//   quantize_kernel    grid (ceil(max(Nq,Nk)/64), B*H, 3 at D = 128, 1 at
+//                      D = 64): one 64-row tile of one tensor per CTA at
+//                      D = 128, of all three at D = 64; group amax via warp
+//                      shuffles + shared memory, scales computed once per
+//                      group or row; V codes transposed to [D, keys] through
+//                      shared memory so the attention kernel's PV operand is
+//                      K-major.
 #pragma once
 
 #include <cuda_bf16.h>
